@@ -1,0 +1,398 @@
+"""Benchmark of the gated-GQA attention hot path (BASELINE.json metric:
+decode attention µs/layer at 32K context and prefill attention TFLOP/s, as a
+fraction of the HBM / tensor-core roofline).
+
+Default workload (one "step"): one token of M=1 decode through the 16
+full-attention layers of the hybrid decoder, every layer with its own bf16 KV
+cache of 32768 positions (the 32K-context decode of the metric; 16 x 134 MB of
+KV, larger than the 126 MB L2, so no flush is needed). value = µs per layer.
+The same run measures config 2 (4096-token prefill in 8 chunks of 512) and
+reports it under "prefill".
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload decode32k|batched|longctx]
+
+N > 1 runs under torchrun, one rank per GPU; decode32k shards independent
+sequences (one per rank, weak scaling, no collective).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for sub in ("lisa-rs_b200", "oracle"):
+    sys.path.insert(0, os.path.join(ROOT, sub))
+
+METRIC = "decode attn µs/layer @32K ctx & prefill attn TFLOP/s, % of HBM/TC roofline"
+UNIT = "µs/layer"
+QH, KVH, HD = 24, 4, 256
+QROW, KROW, OROW = QH * 512, KVH * HD, QH * HD
+LAYERS = 16
+CTX = 32768
+PREFILL_TOKENS, PREFILL_CHUNK = 4096, 512
+PREFILL_FLOP = 4 * QH * HD * sum(range(1, PREFILL_TOKENS + 1))  # causal-exact QK^T + PV
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def decode_bytes(ctx: int, rows: int) -> int:
+    """Algorithmic HBM bytes of one decode layer: the K and V cache read
+    (4 heads x ctx x 256 x 2 B x 2 = 4096 B/token), the q/gate, k, v f32 inputs
+    read, the gated bf16 output written and the appended K/V rows written."""
+    return 4096 * ctx + rows * (QROW * 4 + 2 * KROW * 4 + OROW * 2 + 2 * KROW * 2)
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+def dist_setup():
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def timed(fn, steps, warmup, world, stream):
+    """W untimed steps, then K steps bracketed by barrier + synchronize, timed
+    with CUDA events on the launching stream; returns max-over-ranks ms."""
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    return max_over_ranks(e0.elapsed_time(e1), world)
+
+
+def make_weights(gen, n):
+    import torch
+
+    import lisa_attn
+
+    ws = []
+    for _ in range(n):
+        qn = (1 + 0.02 * torch.randn(HD, generator=gen, device="cuda")).to(torch.bfloat16)
+        kn = (1 + 0.02 * torch.randn(HD, generator=gen, device="cuda")).to(torch.bfloat16)
+        ws.append(lisa_attn.AttentionWeights(qn, kn))
+    return ws
+
+
+def fill_caches(runner, gen, layers, filled):
+    import torch
+
+    for layer in range(layers):
+        kc, vc = runner.kv_cache(layer)
+        for c in (kc, vc):
+            for h in range(KVH):
+                c[h, :filled].copy_(torch.randn((filled, HD), generator=gen, device="cuda").to(torch.bfloat16))
+    torch.cuda.synchronize()
+
+
+def bench_decode32k(args, rank, world, local):
+    import torch
+
+    import lisa_attn
+
+    stream = torch.cuda.current_stream()
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(0x5EED + 3 + rank)
+    runner = lisa_attn.AttnRunner(LAYERS, CTX)
+    fill_caches(runner, gen, LAYERS, CTX - 1)
+    ws = make_weights(gen, LAYERS)
+    base = CTX - 1
+    qs = [torch.randn((1, QROW), generator=gen, device="cuda") for _ in range(LAYERS)]
+    ks = [torch.randn((1, KROW), generator=gen, device="cuda") for _ in range(LAYERS)]
+    vs = [torch.randn((1, KROW), generator=gen, device="cuda") for _ in range(LAYERS)]
+    outs = [torch.empty((1, OROW), dtype=torch.bfloat16, device="cuda") for _ in range(LAYERS)]
+
+    def step():
+        for layer in range(LAYERS):
+            runner.decode_layer(layer, base, 1, qs[layer], ks[layer], vs[layer], ws[layer], outs[layer], stream)
+
+    with ClockSampler(local) as clk:
+        ms = timed(step, args.steps, args.warmup, world, stream)
+    # per-launch duration of the layer call (split-KV kernel + its combine)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(LAYERS)]
+    per_layer = []
+    for _ in range(max(1, args.steps // 2)):
+        for layer in range(LAYERS):
+            evs[layer][0].record(stream)
+            runner.decode_layer(layer, base, 1, qs[layer], ks[layer], vs[layer], ws[layer], outs[layer], stream)
+            evs[layer][1].record(stream)
+        torch.cuda.synchronize()
+        per_layer += [a.elapsed_time(b) for a, b in evs]
+    layer_ms = max_over_ranks(statistics.mean(per_layer), world)
+
+    # end to end through the public API with pinned host buffers
+    hq = [q.cpu().pin_memory() for q in qs]
+    hk = [k.cpu().pin_memory() for k in ks]
+    hv = [v.cpu().pin_memory() for v in vs]
+    hout = [torch.empty((1, OROW), dtype=torch.bfloat16).pin_memory() for _ in range(LAYERS)]
+
+    def step_e2e():
+        for layer in range(LAYERS):
+            qs[layer].copy_(hq[layer], non_blocking=True)
+            ks[layer].copy_(hk[layer], non_blocking=True)
+            vs[layer].copy_(hv[layer], non_blocking=True)
+            runner.decode_layer(layer, base, 1, qs[layer], ks[layer], vs[layer], ws[layer], outs[layer], stream)
+            hout[layer].copy_(outs[layer], non_blocking=True)
+
+    ms_e2e = timed(step_e2e, args.steps, args.warmup, world, stream)
+    runner.check_device_error()
+    return {"ms": ms, "layer_ms": layer_ms, "ms_e2e": ms_e2e, "clocks": clk.summary(),
+            "h2d": LAYERS * (QROW + 2 * KROW) * 4, "d2h": LAYERS * OROW * 2}
+
+
+def bench_prefill(args, world):
+    import torch
+
+    import lisa_attn
+
+    stream = torch.cuda.current_stream()
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(0x5EED + 2)
+    runner = lisa_attn.AttnRunner(1, PREFILL_TOKENS)
+    w = make_weights(gen, 1)[0]
+    q = torch.randn((PREFILL_TOKENS, QROW), generator=gen, device="cuda").to(torch.bfloat16)
+    k = torch.randn((PREFILL_TOKENS, KROW), generator=gen, device="cuda").to(torch.bfloat16)
+    v = torch.randn((PREFILL_TOKENS, KROW), generator=gen, device="cuda").to(torch.bfloat16)
+    out = torch.empty((PREFILL_TOKENS, OROW), dtype=torch.bfloat16, device="cuda")
+    chunks = [(c * PREFILL_CHUNK, PREFILL_CHUNK) for c in range(PREFILL_TOKENS // PREFILL_CHUNK)]
+
+    def step():
+        for b, m in chunks:
+            runner.prefill_layer(0, b, m, q[b:b + m], k[b:b + m], v[b:b + m], w, out[b:b + m], stream)
+
+    ms = timed(step, args.steps, args.warmup, world, stream)
+    runner.check_device_error()
+    return ms
+
+
+def cpu_baseline_decode(seconds: float = 8.0, threads: int | None = None):
+    """The oracle (CPU restatement of the reference shaders) on one decode layer
+    at ctx 32768, all host threads; returns (µs/layer, threads, reps)."""
+    import numpy as np
+
+    import oracle as O
+
+    if threads:
+        O.set_num_threads(threads)
+    rng = np.random.default_rng(0x5EED)
+    qn = O.f32_to_bf16((1 + 0.02 * rng.standard_normal(HD)).astype(np.float32))
+    kn = O.f32_to_bf16((1 + 0.02 * rng.standard_normal(HD)).astype(np.float32))
+    kc = O.f32_to_bf16(rng.standard_normal((KVH, CTX, HD)).astype(np.float32))
+    vc = O.f32_to_bf16(rng.standard_normal((KVH, CTX, HD)).astype(np.float32))
+    q = rng.standard_normal((1, QROW)).astype(np.float32)
+    k = rng.standard_normal((1, KROW)).astype(np.float32)
+    v = rng.standard_normal((1, KROW)).astype(np.float32)
+    times = []
+    t_end = time.perf_counter() + seconds
+    while time.perf_counter() < t_end or len(times) < 2:
+        t0 = time.perf_counter()
+        O.attention_layer(q, k, v, CTX - 1, qn, kn, kc, vc, sliced=True)
+        times.append(time.perf_counter() - t0)
+    return statistics.median(times) * 1e6, O.num_threads(), len(times)
+
+
+def emit(line: dict) -> None:
+    print(json.dumps(line), flush=True)
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's attention math on the host cores (the
+    oracle port: lisa-rs is Metal-only and its Rust cannot be built here), one
+    32K decode layer per step, on rank 0 only."""
+    if rank != 0:
+        return
+    import oracle as O
+
+    threads = os.cpu_count() or 1
+    O.set_num_threads(threads)
+    us, nthr, _ = cpu_baseline_decode(seconds=0.1, threads=threads)  # warm-up (page in, OpenMP pool)
+    samples = []
+    for _ in range(max(0, args.warmup - 1)):
+        cpu_baseline_decode(seconds=0.0, threads=threads)
+    for _ in range(args.steps):
+        us, nthr, _ = cpu_baseline_decode(seconds=0.0, threads=threads)
+        samples.append(us)
+    value = statistics.mean(samples)
+    sample = f"one M=1 decode layer at ctx {CTX} per step (1/16 of a decode32k step), oracle port, {nthr} threads"
+    emit({"impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": args.gpus,
+          "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(value / 1000, 3),
+          "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+          "config": {"workload": "decode32k", "ctx": CTX, "rows": 1, "layers_per_step": 1},
+          "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": nthr, "kind": "port", "sample": sample},
+          "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="decode32k", choices=["decode32k"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        run_reference(args, rank, world)
+        return
+
+    import torch
+
+    rank, world, local = dist_setup()
+    pk = peaks()
+    r = bench_decode32k(args, rank, world, local)
+    pf_ms = bench_prefill(args, world)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        us, nthr, reps = cpu_baseline_decode(seconds=10.0)
+        cpu = {"value": round(us, 2), "unit": UNIT, "cores": nthr, "kind": "port",
+               "sample": f"{reps} oracle runs of one M=1 decode layer at ctx {CTX} (median)"}
+    if rank != 0:
+        return
+    layers_total = LAYERS * world
+    value = r["ms"] * 1000.0 / args.steps / layers_total  # aggregate µs per sequence-layer
+    e2e = r["ms_e2e"] * 1000.0 / args.steps / layers_total
+    layer_bytes = decode_bytes(CTX, 1)
+    achieved = layer_bytes / (r["layer_ms"] * 1e-3) / 1e9
+    pf_tflops = PREFILL_FLOP / (pf_ms / args.steps * 1e-3) / 1e12
+    emit({
+        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(r["ms"] / args.steps, 4), "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "decode32k: M=1 decode, ctx 32768, 16 stacked attention layers per step, "
+                               "one sequence per GPU", "ctx": CTX, "rows": 1, "layers": LAYERS,
+                   "sequences": world, "parallelism": f"sequences sharded, dp{world}, no collective",
+                   "l2": "inputs larger than L2 (16 x 134 MB KV per step)"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None, "peak_source": pk["source"],
+                     "kernel": "decode_split_kernel<1> + decode_combine_kernel (one layer call)",
+                     "algorithmic_bytes": layer_bytes, "layer_us": round(r["layer_ms"] * 1000, 3)},
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(e2e, 3), "unit": UNIT, "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
+        "gpu_launches": 2 * LAYERS * args.steps,
+        "clocks": r["clocks"],
+        "prefill": {"workload": "config 2: 4096 tokens, 8 chunks of 512, one layer", "ms": round(pf_ms / args.steps, 4),
+                    "tflops": round(pf_tflops, 2), "flop": PREFILL_FLOP,
+                    "frac_burst": round(pf_tflops / pk["bf16_tflops"], 4),
+                    "frac_sustained": round(pf_tflops / pk["bf16_tflops_sustained"], 4),
+                    "gpu_launches_per_step": 2 * (PREFILL_TOKENS // PREFILL_CHUNK)},
+    })
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

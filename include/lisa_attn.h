@@ -1,0 +1,187 @@
+/*
+ * lisa_attn.h — C ABI of the B200 (sm_100a) gated-GQA full-attention path.
+ *
+ * The layer is the full-attention layer of the lisa-rs Qwen3.x hybrid decoder
+ * (every 4th layer, src/model/mod.rs:16-22): 24 query heads, 4 KV heads,
+ * head_dim 256, per-head q/k RMSNorm (eps 1e-6), partial NeoX RoPE on dims
+ * 0..63 with theta 1e7, a bf16 KV-cache append, causal softmax(QK^T/16)V with
+ * f32 accumulation, and a sigmoid output gate (src/kernels/shaders/
+ * attention.metal:1-27).
+ *
+ * In lisa-rs there is no FFI for this path: it is the private methods
+ * QwenRunner::encode_attention (src/model/runner.rs:1426-1592),
+ * QwenRunner::encode_prefill_attention (runner.rs:1962-2062) and the KV
+ * position contract (runner.rs:423-503, 911-944, 2376-2545). Each entry point
+ * below names the reference code it replaces. A Rust `extern "C"` block that
+ * binds these declarations is given in INTEGRATION.md.
+ *
+ * Conventions
+ *   - Every entry point returns an int status (LISA_OK or a negative code).
+ *     Invalid arguments are rejected before anything is launched; no call is a
+ *     silent no-op (the reference kernels silently return when out of range,
+ *     attention.metal:172/294/415/450/564).
+ *   - All tensor pointers are CUDA device pointers unless a name says "host".
+ *     The caller owns inputs and outputs; a context owns its KV cache and its
+ *     scratch memory.
+ *   - Work is ordered on the `stream` argument (a cudaStream_t passed as
+ *     void*; NULL = legacy default stream). A context is not thread-safe: use
+ *     one context per thread or a lock, as lisa-rs serialises its runner
+ *     behind a Mutex (src/serve/mod.rs:37-38).
+ *   - Layouts (row-major, elements):
+ *       q_gate  [rows][24][512]  per head: 256 query values then 256 gate values
+ *                                (the q_proj output, runner.rs:204-209)
+ *       k, v    [rows][4][256]   (k_proj / v_proj outputs)
+ *       norm weights  bf16 [256]
+ *       gated_out     bf16 [rows][24*256]  (the o_proj input, runner.rs:1574-1590)
+ *       KV cache      bf16 [layer][4][capacity][256], K and V separately
+ *                     (runner.rs:384-390, 1463-1464)
+ *     q_gate/k/v are f32 (LISA_DTYPE_F32, the QMV/GEMM output type of the
+ *     reference) or bf16 (LISA_DTYPE_BF16). The reference rounds them to bf16
+ *     before use (attention.metal:40-42), so both give identical results.
+ */
+#ifndef LISA_ATTN_H
+#define LISA_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LISA_ATTN_Q_HEADS 24
+#define LISA_ATTN_KV_HEADS 4
+#define LISA_ATTN_HEAD_DIM 256
+#define LISA_ATTN_ROPE_DIM 64
+#define LISA_ATTN_PREFILL_MAX_ROWS 512 /* PREFILL_BATCH, runner.rs:48-51 */
+
+/* Status codes. */
+#define LISA_OK 0
+#define LISA_EINVAL (-22)   /* bad argument: null pointer, rows, layer, dtype */
+#define LISA_ENOSPC (-28)   /* base + rows > capacity ("KV capacity exhausted") */
+#define LISA_ESTATE (-71)   /* position contract violated (no pending verify, trim too far) */
+#define LISA_ETIMEOUT (-62) /* a device-side bounded wait gave up (error flag set) */
+#define LISA_ECUDA (-1000)  /* a CUDA runtime/driver call failed */
+
+/* Input element types of q_gate / k / v. */
+#define LISA_DTYPE_F32 0
+#define LISA_DTYPE_BF16 1
+
+typedef struct lisa_attn_ctx lisa_attn_ctx;
+
+/* ---- context ------------------------------------------------------------
+ * Replaces the KV-cache allocation of QwenRunner::load (runner.rs:384-390) and
+ * MtpRunner::load (runner.rs:2455-2470): n_layers attention layers (16 for the
+ * target, 1 for the MTP drafter), each with K and V caches of
+ * [4][capacity][256] bf16, zero-filled, position 0. Also allocates the split-KV
+ * scratch and a device error flag. capacity must be in 1..2^31. */
+int lisa_attn_create(int device, int n_layers, uint32_t capacity, lisa_attn_ctx** out);
+int lisa_attn_destroy(lisa_attn_ctx* ctx);
+
+/* Device pointers of one layer's K and V cache ([4][capacity][256] bf16). */
+int lisa_attn_kv_cache(lisa_attn_ctx* ctx, int layer, void** k_cache, void** v_cache);
+uint32_t lisa_attn_capacity(const lisa_attn_ctx* ctx);
+int lisa_attn_n_layers(const lisa_attn_ctx* ctx);
+
+/* ---- per-layer dispatch ---------------------------------------------------
+ * Decode (rows = 1) or MTP verify (rows = 3) of one attention layer at absolute
+ * positions base .. base+rows-1. Replaces encode_attention's attention part
+ * (runner.rs:1439-1590): q norm+RoPE+gate split (attention.metal:118-155,
+ * 245-281), K/V append (158-197, 283-319), split-KV attention and merge
+ * (550-641) and the gate (520-531). Row r attends causally over positions
+ * 0 .. base+r. Rows of a verify are bit-identical to the same rows decoded one
+ * at a time (the invariant tested at tests/attn_sliced.rs:186-187).
+ * Errors: LISA_EINVAL (rows not 1 or 3, bad layer, null pointer, bad dtype),
+ * LISA_ENOSPC (base + rows > capacity). */
+int lisa_attn_decode(lisa_attn_ctx* ctx, int layer, uint32_t base, int rows, int in_dtype,
+                     const void* q_gate, const void* k, const void* v,
+                     const uint16_t* q_norm_w, const uint16_t* k_norm_w, float eps,
+                     uint16_t* gated_out, void* stream);
+
+/* Chunked prefill of one attention layer: rows (1..512) prompt rows at
+ * positions base .. base+rows-1, causal over the whole cached prefix.
+ * Replaces encode_prefill_attention's attention part (runner.rs:1976-2060):
+ * attention.metal:364-480 and 520-531. Errors as lisa_attn_decode, with rows
+ * allowed in 1..512. */
+int lisa_attn_prefill_chunk(lisa_attn_ctx* ctx, int layer, uint32_t base, int rows, int in_dtype,
+                            const void* q_gate, const void* k, const void* v,
+                            const uint16_t* q_norm_w, const uint16_t* k_norm_w, float eps,
+                            uint16_t* gated_out, void* stream);
+
+/* ---- position contract ----------------------------------------------------
+ * The logical KV length. Entries past it stay in the cache and are overwritten
+ * by the next append; nothing is cleared (runner.rs:474-503, 2522-2545). */
+uint32_t lisa_attn_position(const lisa_attn_ctx* ctx);
+
+/* End of one forward over all layers: position += rows (runner.rs:589 for
+ * rows = 1, runner.rs:2225 for a prefill chunk). rows == 3 is a block-3
+ * verify: the base is remembered for lisa_attn_commit_verified_prefix
+ * (runner.rs:906-907). LISA_ENOSPC if position + rows > capacity. */
+int lisa_attn_advance(lisa_attn_ctx* ctx, int rows, int is_verify);
+
+/* QwenRunner::commit_verified_prefix (runner.rs:911-944): position =
+ * verify_base + rows, rows in 1..3. LISA_ESTATE if no verify is pending,
+ * LISA_EINVAL for rows outside 1..3. The KV cache is not touched. */
+int lisa_attn_commit_verified_prefix(lisa_attn_ctx* ctx, int rows);
+
+/* MtpRunner::trim_state (runner.rs:2522-2531): position -= count;
+ * LISA_ESTATE if count > position. */
+int lisa_attn_trim_state(lisa_attn_ctx* ctx, uint32_t count);
+
+/* MtpRunner::set_position (runner.rs:2536-2545): only moves backwards;
+ * LISA_ESTATE if position > current position. */
+int lisa_attn_set_position(lisa_attn_ctx* ctx, uint32_t position);
+
+/* QwenRunner::restore_state's position part (runner.rs:476-503): any position
+ * up to capacity (LISA_ENOSPC beyond it); clears a pending verify. */
+int lisa_attn_restore_position(lisa_attn_ctx* ctx, uint32_t position);
+
+/* reset_state (runner.rs:423-444, 2505-2516): zero the whole KV cache,
+ * position 0, no pending verify. Stream-ordered. */
+int lisa_attn_reset_state(lisa_attn_ctx* ctx, void* stream);
+
+/* MtpCheckpoint (runner.rs:2376-2441): copy all layers' K then V caches
+ * (2 * n_layers * 4 * capacity * 256 * 2 bytes, lisa_attn_snapshot_bytes) to a
+ * caller-owned device buffer, or back, plus the position. Stream-ordered. */
+size_t lisa_attn_snapshot_bytes(const lisa_attn_ctx* ctx);
+int lisa_attn_kv_snapshot(lisa_attn_ctx* ctx, void* dst, size_t dst_bytes, uint32_t* position_out,
+                          void* stream);
+int lisa_attn_kv_restore(lisa_attn_ctx* ctx, const void* src, size_t src_bytes, uint32_t position,
+                         void* stream);
+
+/* Device-side error flag of the context (bounded waits that gave up).
+ * Synchronises the context's device; returns LISA_OK, LISA_ETIMEOUT or
+ * LISA_ECUDA, and clears the flag. */
+int lisa_attn_check_device_error(lisa_attn_ctx* ctx);
+
+/* ---- split-KV window entry points (multi-GPU) ------------------------------
+ * No lisa-rs counterpart: lisa-rs drives one GPU. These let one long sequence's
+ * KV be split along the position axis over several GPUs. A window holds cache
+ * positions [kv_lo, kv_lo + window_rows) of one layer at k_cache / v_cache
+ * ([4][window_rows][256] bf16, row i = position kv_lo + i). The call appends
+ * the new rows that fall inside the window, attends rows 0..rows-1 over the
+ * window's positions below base+r+1, and writes one partial per (row, head):
+ * part_o f32 [rows][24][256] (normalised), part_ml f32 [rows][24][2] = {max
+ * score, sum of exp(score - max)}. A window holding no position for a row gives
+ * max = -inf, sum = 0. workspace: lisa_attn_window_workspace_bytes(window_rows,
+ * rows) bytes of device memory, 256-byte aligned. */
+size_t lisa_attn_window_workspace_bytes(uint32_t window_rows, int rows);
+int lisa_attn_decode_window(void* k_cache, void* v_cache, uint32_t window_rows, uint32_t kv_lo,
+                            uint32_t base, int rows, int in_dtype, const void* q_gate,
+                            const void* k, const void* v, const uint16_t* q_norm_w,
+                            const uint16_t* k_norm_w, float eps, float* part_o, float* part_ml,
+                            void* workspace, size_t workspace_bytes, void* stream);
+
+/* Merge n_parts window partials (stacked: part_o [n_parts][rows][24][256],
+ * part_ml [n_parts][rows][24][2]) by log-sum-exp and apply the sigmoid gate
+ * taken from q_gate: gated_out bf16 [rows][24*256]. */
+int lisa_attn_merge_windows(int n_parts, int rows, const float* part_o, const float* part_ml,
+                            int in_dtype, const void* q_gate, uint16_t* gated_out, void* stream);
+
+/* Library build identification (for tests: the .so in use). */
+const char* lisa_attn_build_info(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LISA_ATTN_H */

@@ -1,0 +1,174 @@
+// common.cuh — constants and hand-written PTX helpers for the sm_100a
+// attention kernels: bf16 conversion, mbarriers with bounded waits, TMA
+// (cp.async.bulk.tensor, no multicast), ldmatrix / mma.sync / movmatrix.
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace lisa {
+
+// Head geometry of the lisa-rs full-attention layer (attention.metal:13-23).
+constexpr int QH = 24;         // query heads
+constexpr int KVH = 4;         // KV heads
+constexpr int GQA = QH / KVH;  // 6 query heads share one KV head
+constexpr int HD = 256;        // head dim
+constexpr int ROT_PAIRS = 32;  // RoPE on dims [0, 64): pairs (j, j+32)
+constexpr int QROW = QH * 512; // q_proj row: per head 256 query + 256 gate
+constexpr int KROW = KVH * HD;
+constexpr int OROW = QH * HD;
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr float SCALE = 0.0625f;  // 1/sqrt(256)
+
+// Device error codes written to the context's error word.
+constexpr int ERR_TIMEOUT_FULL = 1;
+constexpr int ERR_TIMEOUT_EMPTY = 2;
+constexpr int ERR_TIMEOUT_MMA = 3;
+
+// Bounded waits give up after this many nanoseconds of %globaltimer.
+constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ float bf16_bits_to_f32(uint32_t b) { return __uint_as_float(b << 16); }
+
+__device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+
+__device__ __forceinline__ float round_bf16(float f) { return __bfloat162float(__float2bfloat16_rn(f)); }
+
+// Two floats -> packed bf16x2 (lo in bits 0..15), round to nearest even.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Reads element i of an f32 or bf16 input array as f32 rounded to bf16 — the
+// reference rounds every projection output to bf16 first (attention.metal:40-42).
+__device__ __forceinline__ float load_in_bf16(const void* p, size_t i, int is_bf16) {
+  if (is_bf16) return bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(p)[i]);
+  return round_bf16(reinterpret_cast<const float*>(p)[i]);
+}
+
+// RoPE inverse frequency 1/theta^(2j/64), theta = 1e7, evaluated in double and
+// rounded to f32; the angle is the reference's f32 product pos * inv_freq
+// (attention.metal:147); cos/sin of that f32 angle are evaluated in double.
+__device__ __forceinline__ void rope_cs(uint32_t pos, int j, float& c, float& s) {
+  const float inv = (float)(1.0 / pow(1.0e7, (double)(2 * j) / 64.0));
+  const float angle = (float)pos * inv;
+  double sd, cd;
+  sincos((double)angle, &sd, &cd);
+  c = (float)cd;
+  s = (float)sd;
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---- mbarrier ---------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Waits for the phase with the given parity to complete. Gives up after
+// WAIT_LIMIT_NS, records `code` in *err and returns false.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (global_timer_ns() - t0 > WAIT_LIMIT_NS) {
+      if (err) atomicExch(err, code);
+      return false;
+    }
+  }
+}
+
+// Order this thread's generic-proxy shared-memory writes before later
+// async-proxy (TMA) accesses of the same memory.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---- TMA (tiled, no multicast) -----------------------------------------------
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                            int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// ---- warp-level tensor core (legacy mma.sync; used by the HBM-bound decode) ---
+__device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                            uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                                  uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+// D(16x8 f32) += A(16x16 bf16, row) * B(16x8 bf16, col)
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                               uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
+// Programmatic dependent launch.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait_primary() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Byte offset of (row, 16-byte chunk) inside a TMA SWIZZLE_128B tile whose
+// rows are 128 bytes and whose base is 1024-byte aligned.
+__device__ __forceinline__ uint32_t swz128(uint32_t row, uint32_t chunk) {
+  return row * 128u + ((chunk ^ (row & 7u)) << 4);
+}
+
+}  // namespace lisa

@@ -1,0 +1,41 @@
+// prefill.cuh — launch interface of the chunked-prefill attention kernels.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+// Encodes a TMA map over a bf16 [planes][window_rows][256] array (a cache
+// window has 4 planes): dims {256, rows, planes}, boxes {64, box_rows, 1},
+// SWIZZLE_128B. Defined in runtime.cu.
+int lisa_encode_kv_map(CUtensorMap* map, const void* base, uint32_t rows, uint32_t window_rows, uint32_t box_rows,
+                       uint32_t planes);
+
+namespace lisa {
+
+constexpr int PF_MAX_ROWS = 512;
+
+struct PrefillParams {
+  const void* q_gate;  // [rows][24][512]
+  const void* k_in;    // [rows][4][256]
+  const void* v_in;
+  int in_bf16;
+  const uint16_t* q_norm_w;
+  const uint16_t* k_norm_w;
+  float eps;
+  uint16_t* k_cache;  // [4][capacity][256]
+  uint16_t* v_cache;
+  uint32_t capacity;
+  uint32_t base;      // position of row 0
+  int rows;           // 1..512
+  uint16_t* q_ws;     // workspace: normalised query, bf16 [24][512][256]
+  uint16_t* gated_out;  // [rows][6144]
+  int* err;
+};
+
+// Bytes of device workspace launch_prefill needs.
+size_t prefill_workspace_bytes();
+
+// Prologue (q norm/RoPE into q_ws, K/V append) then the tcgen05 attention.
+cudaError_t launch_prefill(const PrefillParams& p, int num_sms, cudaStream_t stream);
+
+}  // namespace lisa

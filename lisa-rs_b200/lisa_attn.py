@@ -1,0 +1,288 @@
+"""Host-side mirror of the lisa-rs attention dispatch over the C ABI in
+include/lisa_attn.h (liblisa_attn.so, built for sm_100a).
+
+``AttnRunner`` keeps the method names and position semantics of the
+attention slice of ``QwenRunner`` / ``MtpRunner`` (lisa-rs
+src/model/runner.rs): ``forward_decode`` / ``verify_block3`` /
+``forward_prefill`` run one attention layer, ``advance`` ends a forward,
+``commit_verified_prefix``, ``trim_state``, ``set_position``,
+``restore_state``, ``reset_state`` and ``checkpoint_state`` follow
+runner.rs:423-503, 911-944 and 2376-2545. Errors raise ``LisaError`` with the
+C status, as the reference returns ``Err(String)``.
+
+Tensors are torch CUDA tensors (torch is only the device-memory allocator
+here). There is no CPU path: if the CUDA library is missing, loading fails.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "liblisa_attn.so")
+
+QH, KVH, HD = 24, 4, 256
+QROW, KROW, OROW = QH * 512, KVH * HD, QH * HD
+PREFILL_MAX_ROWS = 512
+
+OK, EINVAL, ENOSPC, ESTATE, ETIMEOUT, ECUDA = 0, -22, -28, -71, -62, -1000
+DTYPE_F32, DTYPE_BF16 = 0, 1
+_NAMES = {EINVAL: "EINVAL", ENOSPC: "ENOSPC", ESTATE: "ESTATE", ETIMEOUT: "ETIMEOUT", ECUDA: "ECUDA"}
+
+# name -> (restype, argtypes); mirrors include/lisa_attn.h
+_P, _u32, _i32, _f32, _sz = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
+SIGNATURES = {
+    "lisa_attn_create": (_i32, [_i32, _i32, _u32, ctypes.POINTER(_P)]),
+    "lisa_attn_destroy": (_i32, [_P]),
+    "lisa_attn_kv_cache": (_i32, [_P, _i32, ctypes.POINTER(_P), ctypes.POINTER(_P)]),
+    "lisa_attn_capacity": (_u32, [_P]),
+    "lisa_attn_n_layers": (_i32, [_P]),
+    "lisa_attn_decode": (_i32, [_P, _i32, _u32, _i32, _i32, _P, _P, _P, _P, _P, _f32, _P, _P]),
+    "lisa_attn_prefill_chunk": (_i32, [_P, _i32, _u32, _i32, _i32, _P, _P, _P, _P, _P, _f32, _P, _P]),
+    "lisa_attn_position": (_u32, [_P]),
+    "lisa_attn_advance": (_i32, [_P, _i32, _i32]),
+    "lisa_attn_commit_verified_prefix": (_i32, [_P, _i32]),
+    "lisa_attn_trim_state": (_i32, [_P, _u32]),
+    "lisa_attn_set_position": (_i32, [_P, _u32]),
+    "lisa_attn_restore_position": (_i32, [_P, _u32]),
+    "lisa_attn_reset_state": (_i32, [_P, _P]),
+    "lisa_attn_snapshot_bytes": (_sz, [_P]),
+    "lisa_attn_kv_snapshot": (_i32, [_P, _P, _sz, ctypes.POINTER(_u32), _P]),
+    "lisa_attn_kv_restore": (_i32, [_P, _P, _sz, _u32, _P]),
+    "lisa_attn_check_device_error": (_i32, [_P]),
+    "lisa_attn_window_workspace_bytes": (_sz, [_u32, _i32]),
+    "lisa_attn_decode_window": (_i32, [_P, _P, _u32, _u32, _u32, _i32, _i32, _P, _P, _P, _P, _P, _f32, _P, _P,
+                                       _P, _sz, _P]),
+    "lisa_attn_merge_windows": (_i32, [_i32, _i32, _P, _P, _i32, _P, _P, _P]),
+    "lisa_attn_build_info": (ctypes.c_char_p, []),
+}
+
+_lib = None
+
+
+class LisaError(RuntimeError):
+    def __init__(self, fn: str, status: int):
+        super().__init__(f"{fn} failed: {_NAMES.get(status, status)} ({status})")
+        self.status = status
+
+
+def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Loads liblisa_attn.so and binds every declared entry point. Raises
+    OSError if the library has not been built (no fallback exists)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise OSError(f"{path} not built; run `make -C {_HERE}` (or __graft_entry__.build())")
+    lib = ctypes.CDLL(path)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def _check(fn: str, status: int) -> None:
+    if status != OK:
+        raise LisaError(fn, status)
+
+
+def _ptr(t) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _dtype_code(t) -> int:
+    import torch
+
+    if t.dtype == torch.float32:
+        return DTYPE_F32
+    if t.dtype == torch.bfloat16:
+        return DTYPE_BF16
+    raise TypeError(f"q/k/v must be float32 or bfloat16, got {t.dtype}")
+
+
+def _stream_ptr(stream) -> int | None:
+    import torch
+
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+class AttentionWeights:
+    """The attention-layer weights the path reads: q_norm and k_norm gains
+    (bf16 [256]); cf. AttentionWeights in runner.rs:93-101."""
+
+    def __init__(self, q_norm, k_norm):
+        import torch
+
+        assert q_norm.dtype == torch.bfloat16 and k_norm.dtype == torch.bfloat16
+        assert q_norm.numel() == HD and k_norm.numel() == HD
+        self.q_norm = q_norm.contiguous()
+        self.k_norm = k_norm.contiguous()
+
+
+class AttnRunner:
+    """KV cache + position contract of the attention layers of one model
+    (n_layers = 16 for the target, 1 for the MTP drafter)."""
+
+    def __init__(self, n_layers: int, capacity: int, device: int | None = None, eps: float = 1e-6):
+        import torch
+
+        self.lib = load_library()
+        self.device = torch.cuda.current_device() if device is None else device
+        self.eps = eps
+        h = _P()
+        _check("lisa_attn_create", self.lib.lisa_attn_create(self.device, n_layers, capacity, ctypes.byref(h)))
+        self._h = h
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            self.lib.lisa_attn_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ---- state ----
+    @property
+    def handle(self):
+        return self._h
+
+    @property
+    def capacity(self) -> int:
+        return self.lib.lisa_attn_capacity(self._h)
+
+    @property
+    def n_layers(self) -> int:
+        return self.lib.lisa_attn_n_layers(self._h)
+
+    def position(self) -> int:
+        return self.lib.lisa_attn_position(self._h)
+
+    def kv_cache(self, layer: int):
+        """(k, v) as torch bf16 views [4, capacity, 256] of the layer's cache."""
+        import torch
+
+        k, v = _P(), _P()
+        _check("lisa_attn_kv_cache", self.lib.lisa_attn_kv_cache(self._h, layer, ctypes.byref(k), ctypes.byref(v)))
+        return _wrap_device(k.value, (KVH, self.capacity, HD), self.device), _wrap_device(
+            v.value, (KVH, self.capacity, HD), self.device)
+
+    # ---- dispatch ----
+    def _layer_call(self, fn, layer, base, rows, q_gate, k, v, w: AttentionWeights, out, stream):
+        import torch
+
+        dt = _dtype_code(q_gate)
+        assert k.dtype == q_gate.dtype and v.dtype == q_gate.dtype
+        for t in (q_gate, k, v):
+            assert t.is_cuda and t.is_contiguous()
+        assert q_gate.numel() == rows * QROW and k.numel() == rows * KROW and v.numel() == rows * KROW
+        if out is None:
+            out = torch.empty((rows, OROW), dtype=torch.bfloat16, device=q_gate.device)
+        status = getattr(self.lib, fn)(self._h, layer, base, rows, dt, _ptr(q_gate), _ptr(k), _ptr(v),
+                                       _ptr(w.q_norm), _ptr(w.k_norm), self.eps, _ptr(out), _stream_ptr(stream))
+        _check(fn, status)
+        return out
+
+    def decode_layer(self, layer, base, rows, q_gate, k, v, w, out=None, stream=None):
+        """One attention layer at explicit base (rows 1 or 3)."""
+        return self._layer_call("lisa_attn_decode", layer, base, rows, q_gate, k, v, w, out, stream)
+
+    def prefill_layer(self, layer, base, rows, q_gate, k, v, w, out=None, stream=None):
+        return self._layer_call("lisa_attn_prefill_chunk", layer, base, rows, q_gate, k, v, w, out, stream)
+
+    def forward_decode(self, layer, q_gate, k, v, w, out=None, stream=None):
+        """encode_attention with batch 1 at the current position (runner.rs:1426)."""
+        return self.decode_layer(layer, self.position(), 1, q_gate, k, v, w, out, stream)
+
+    def verify_block3(self, layer, q_gate, k, v, w, out=None, stream=None):
+        """encode_attention with batch 3 at the current position."""
+        return self.decode_layer(layer, self.position(), 3, q_gate, k, v, w, out, stream)
+
+    def forward_prefill(self, layer, q_gate, k, v, w, out=None, stream=None):
+        """encode_prefill_attention for one chunk of <= 512 rows (runner.rs:1962)."""
+        rows = q_gate.numel() // QROW
+        return self.prefill_layer(layer, self.position(), rows, q_gate, k, v, w, out, stream)
+
+    def advance(self, rows: int, verify: bool = False) -> None:
+        _check("lisa_attn_advance", self.lib.lisa_attn_advance(self._h, rows, int(verify)))
+
+    def commit_verified_prefix(self, rows: int) -> None:
+        _check("lisa_attn_commit_verified_prefix", self.lib.lisa_attn_commit_verified_prefix(self._h, rows))
+
+    def trim_state(self, count: int) -> None:
+        _check("lisa_attn_trim_state", self.lib.lisa_attn_trim_state(self._h, count))
+
+    def set_position(self, position: int) -> None:
+        _check("lisa_attn_set_position", self.lib.lisa_attn_set_position(self._h, position))
+
+    def restore_position(self, position: int) -> None:
+        _check("lisa_attn_restore_position", self.lib.lisa_attn_restore_position(self._h, position))
+
+    def reset_state(self, stream=None) -> None:
+        _check("lisa_attn_reset_state", self.lib.lisa_attn_reset_state(self._h, _stream_ptr(stream)))
+
+    def checkpoint_state(self, stream=None):
+        """MtpRunner::checkpoint_state: device copy of all K/V + position."""
+        import torch
+
+        n = self.lib.lisa_attn_snapshot_bytes(self._h)
+        buf = torch.empty(n, dtype=torch.uint8, device=f"cuda:{self.device}")
+        pos = _u32()
+        _check("lisa_attn_kv_snapshot",
+               self.lib.lisa_attn_kv_snapshot(self._h, _ptr(buf), n, ctypes.byref(pos), _stream_ptr(stream)))
+        return buf, pos.value
+
+    def restore_state(self, checkpoint, stream=None) -> None:
+        buf, pos = checkpoint
+        _check("lisa_attn_kv_restore",
+               self.lib.lisa_attn_kv_restore(self._h, _ptr(buf), buf.numel(), pos, _stream_ptr(stream)))
+
+    def check_device_error(self) -> None:
+        _check("lisa_attn_check_device_error", self.lib.lisa_attn_check_device_error(self._h))
+
+
+def _wrap_device(ptr: int, shape, device: int):
+    """A torch bf16 tensor view of device memory owned by the library."""
+    import torch
+
+    class _Holder:
+        pass
+
+    n = 1
+    for s in shape:
+        n *= s
+    holder = _Holder()
+    holder.__cuda_array_interface__ = {
+        "shape": (n,), "typestr": "<u2", "data": (ptr, False), "version": 3, "strides": None}
+    with torch.cuda.device(device):
+        t = torch.as_tensor(holder, device=f"cuda:{device}")
+    return t.view(torch.bfloat16).view(*shape)
+
+
+# ---- split-KV windows (multi-GPU long context) --------------------------------
+
+def window_workspace_bytes(window_rows: int, rows: int) -> int:
+    return load_library().lisa_attn_window_workspace_bytes(window_rows, rows)
+
+
+def decode_window(k_cache, v_cache, kv_lo, base, rows, q_gate, k, v, w, part_o, part_ml, workspace,
+                  eps=1e-6, stream=None):
+    lib = load_library()
+    window_rows = k_cache.shape[1]
+    _check("lisa_attn_decode_window",
+           lib.lisa_attn_decode_window(_ptr(k_cache), _ptr(v_cache), window_rows, kv_lo, base, rows,
+                                       _dtype_code(q_gate), _ptr(q_gate), _ptr(k), _ptr(v), _ptr(w.q_norm),
+                                       _ptr(w.k_norm), eps, _ptr(part_o), _ptr(part_ml), _ptr(workspace),
+                                       workspace.numel() * workspace.element_size(), _stream_ptr(stream)))
+
+
+def merge_windows(n_parts, rows, part_o, part_ml, q_gate, out, stream=None):
+    lib = load_library()
+    _check("lisa_attn_merge_windows",
+           lib.lisa_attn_merge_windows(n_parts, rows, _ptr(part_o), _ptr(part_ml), _dtype_code(q_gate),
+                                       _ptr(q_gate), _ptr(out), _stream_ptr(stream)))

@@ -1,0 +1,60 @@
+"""Shared test helpers: seeded synthetic inputs with the BASELINE.json
+distributions, oracle runs, and the north-star tolerance check."""
+from __future__ import annotations
+
+import numpy as np
+
+import oracle as O
+
+QH, KVH, HD = 24, 4, 256
+QROW, KROW, OROW = QH * 512, KVH * HD, QH * HD
+ATOL, RTOL = 8e-3, 1e-2  # north-star tolerance on bf16 outputs
+
+
+def bf16_round(x: np.ndarray) -> np.ndarray:
+    return O.bf16_to_f32(O.f32_to_bf16(np.asarray(x, np.float32)))
+
+
+def norm_weights(rng: np.random.Generator):
+    """1 + N(0, 0.02) as bf16 bits."""
+    qn = O.f32_to_bf16((1.0 + 0.02 * rng.standard_normal(HD)).astype(np.float32))
+    kn = O.f32_to_bf16((1.0 + 0.02 * rng.standard_normal(HD)).astype(np.float32))
+    return qn, kn
+
+
+def layer_inputs(rng: np.random.Generator, rows: int):
+    """q_gate [rows, 12288], k, v [rows, 1024]: N(0,1) rounded to bf16 (f32 arrays)."""
+    q = bf16_round(rng.standard_normal((rows, QROW)).astype(np.float32))
+    k = bf16_round(rng.standard_normal((rows, KROW)).astype(np.float32))
+    v = bf16_round(rng.standard_normal((rows, KROW)).astype(np.float32))
+    return q, k, v
+
+
+def random_cache(rng: np.random.Generator, capacity: int, filled: int):
+    """K/V caches [4, capacity, 256] bf16 bits; rows < filled ~ N(0,1)
+    (post-norm, post-RoPE values drawn directly), the rest zero."""
+    kc = np.zeros((KVH, capacity, HD), np.uint16)
+    vc = np.zeros((KVH, capacity, HD), np.uint16)
+    if filled:
+        kc[:, :filled] = O.f32_to_bf16(rng.standard_normal((KVH, filled, HD)).astype(np.float32))
+        vc[:, :filled] = O.f32_to_bf16(rng.standard_normal((KVH, filled, HD)).astype(np.float32))
+    return kc, vc
+
+
+def assert_close_bf16(got_bits: np.ndarray, want_bits: np.ndarray, what: str = ""):
+    g = O.bf16_to_f32(got_bits).astype(np.float64)
+    w = O.bf16_to_f32(want_bits).astype(np.float64)
+    assert np.all(np.isfinite(g)), f"{what}: non-finite output"
+    err = np.abs(g - w)
+    bad = err > np.maximum(ATOL, RTOL * np.abs(w))
+    assert not bad.any(), (f"{what}: {bad.sum()} of {bad.size} outside tolerance; max abs err "
+                           f"{err.max():.3e} at {np.unravel_index(err.argmax(), err.shape)}")
+    return float(err.max())
+
+
+def argmax_projection(gated_bits: np.ndarray, seed: int = 1234, n_out: int = 1024) -> np.ndarray:
+    """Argmax of a seeded synthetic projection of each row (the north star's
+    exact-argmax check): [rows, 6144] @ W[6144, n_out]."""
+    rng = np.random.default_rng(seed)
+    w = rng.standard_normal((OROW, n_out)).astype(np.float32)
+    return np.argmax(O.bf16_to_f32(gated_bits).reshape(-1, OROW) @ w, axis=1)
