@@ -3,7 +3,7 @@ import numpy as np
 import pytest
 
 import oracle as O
-from helpers import HD, KROW, OROW, QROW, assert_close_bf16, argmax_projection, layer_inputs, norm_weights
+from helpers import HD, KROW, OROW, QROW, assert_close_bf16, assert_argmax_agrees, layer_inputs, norm_weights
 
 pytestmark = pytest.mark.gpu
 
@@ -58,7 +58,7 @@ def test_prefill_matches_oracle(chunks):
         pos += m
     want = np.concatenate(want)
     assert_close_bf16(got, want, f"prefill {chunks}")
-    assert np.array_equal(argmax_projection(got), argmax_projection(want))
+    assert_argmax_agrees(got, want, "argmax")
     gk, gv = read_cache(r, 0)
     assert np.array_equal(gv[:, :n], vc[:, :n])
     kd = np.abs(O.bf16_to_f32(gk[:, :n]) - O.bf16_to_f32(kc[:, :n]))
