@@ -62,6 +62,7 @@ extern "C" {
 #define LISA_ESTATE (-71)   /* position contract violated (no pending verify, trim too far) */
 #define LISA_ETIMEOUT (-62) /* a device-side bounded wait gave up (error flag set) */
 #define LISA_ECUDA (-1000)  /* a CUDA runtime/driver call failed */
+#define LISA_E2BIG (-7)     /* request larger than the fixed scratch of lisa_attn_decode_noalloc */
 
 /* Input element types of q_gate / k / v. */
 #define LISA_DTYPE_F32 0
@@ -177,6 +178,29 @@ int lisa_attn_decode_window(void* k_cache, void* v_cache, uint32_t window_rows, 
  * taken from q_gate: gated_out bf16 [rows][24*256]. */
 int lisa_attn_merge_windows(int n_parts, int rows, const float* part_o, const float* part_ml,
                             int in_dtype, const void* q_gate, uint16_t* gated_out, void* stream);
+
+/* ---- decode without allocation -------------------------------------------
+ * No counterpart in lisa-rs. For callers that may not allocate device memory
+ * while they run: an engine that hands out all of its GPU memory from a pool
+ * reserved at start-up, or a caller whose allocator must not be entered on the
+ * decode path. Same work and results as lisa_attn_decode, but over a KV cache
+ * the caller owns (k_cache / v_cache, [4][capacity][256] bf16, row i =
+ * position i) and with its scratch in a fixed array compiled into the library
+ * (about 12.6 MB per GPU that loads it, held until the process exits), so the
+ * call allocates nothing.
+ *   - base + rows must not exceed LISA_ATTN_NOALLOC_MAX_POSITIONS; larger
+ *     requests return LISA_E2BIG (use lisa_attn_decode for them).
+ *   - The first call on a device looks up the array's device address; make
+ *     that first call before any stream capture on that device.
+ *   - All calls share the one array: calls that can overlap on the GPU (other
+ *     streams, other host threads) race; the caller must serialise them.
+ * Errors otherwise as lisa_attn_decode (LISA_EINVAL, LISA_ENOSPC when
+ * base + rows > capacity). */
+#define LISA_ATTN_NOALLOC_MAX_POSITIONS 16384
+int lisa_attn_decode_noalloc(void* k_cache, void* v_cache, uint32_t capacity, uint32_t base, int rows,
+                             int in_dtype, const void* q_gate, const void* k, const void* v,
+                             const uint16_t* q_norm_w, const uint16_t* k_norm_w, float eps,
+                             uint16_t* gated_out, void* stream);
 
 /* Library build identification (for tests: the .so in use). */
 const char* lisa_attn_build_info(void);

@@ -25,9 +25,10 @@ QH, KVH, HD = 24, 4, 256
 QROW, KROW, OROW = QH * 512, KVH * HD, QH * HD
 PREFILL_MAX_ROWS = 512
 
-OK, EINVAL, ENOSPC, ESTATE, ETIMEOUT, ECUDA = 0, -22, -28, -71, -62, -1000
+OK, EINVAL, ENOSPC, ESTATE, ETIMEOUT, ECUDA, E2BIG = 0, -22, -28, -71, -62, -1000, -7
+NOALLOC_MAX_POSITIONS = 16384
 DTYPE_F32, DTYPE_BF16 = 0, 1
-_NAMES = {EINVAL: "EINVAL", ENOSPC: "ENOSPC", ESTATE: "ESTATE", ETIMEOUT: "ETIMEOUT", ECUDA: "ECUDA"}
+_NAMES = {E2BIG: "E2BIG", EINVAL: "EINVAL", ENOSPC: "ENOSPC", ESTATE: "ESTATE", ETIMEOUT: "ETIMEOUT", ECUDA: "ECUDA"}
 
 # name -> (restype, argtypes); mirrors include/lisa_attn.h
 _P, _u32, _i32, _f32, _sz = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
@@ -54,6 +55,7 @@ SIGNATURES = {
     "lisa_attn_decode_window": (_i32, [_P, _P, _u32, _u32, _u32, _i32, _i32, _P, _P, _P, _P, _P, _f32, _P, _P,
                                        _P, _sz, _P]),
     "lisa_attn_merge_windows": (_i32, [_i32, _i32, _P, _P, _i32, _P, _P, _P]),
+    "lisa_attn_decode_noalloc": (_i32, [_P, _P, _u32, _u32, _i32, _i32, _P, _P, _P, _P, _P, _f32, _P, _P]),
     "lisa_attn_build_info": (ctypes.c_char_p, []),
 }
 
