@@ -71,10 +71,26 @@ class ClockSampler:
         self.proc = None
         self.lines: list[str] = []
 
+    def _fields(self):
+        """The driver names the reasons clocks_event_reasons.* or, on older
+        drivers, clocks_throttle_reasons.*; use whichever it accepts."""
+        for f in (self.FIELDS, self.FIELDS.replace("clocks_event_reasons", "clocks_throttle_reasons")):
+            try:
+                r = subprocess.run(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={f}", "--format=csv,noheader"],
+                                   capture_output=True, text=True, timeout=20)
+                if r.returncode == 0:
+                    return f
+            except Exception:
+                pass
+        return None
+
     def __enter__(self):
         try:
+            fields = self._fields()
+            if fields is None:
+                return self
             self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={fields}", "--format=csv,noheader,nounits",
                  "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -215,6 +231,13 @@ def bench_decode32k(args, rank, world, local):
             runner.decode_layer(layer, base, 1, qs[layer], ks[layer], vs[layer], ws[layer], outs[layer], stream)
 
     with ClockSampler(local) as clk:
+        # keep the GPU under this load long enough for nvidia-smi to sample it
+        # (one step is under a millisecond), then the timed region itself
+        t_end = time.perf_counter() + 1.5
+        while time.perf_counter() < t_end:
+            for _ in range(20):
+                step()
+            torch.cuda.synchronize()
         ms = timed(step, args.steps, args.warmup, world, stream)
     # per-launch duration of the layer call (split-KV kernel + its combine)
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(LAYERS)]

@@ -9,6 +9,11 @@
 
 namespace lisa {
 
+// Host: inv_freq[j] = (float)(1 / 1e7^(2j/64)) for the 32 rotated pairs.
+inline void host_inv_freq(float* inv) {
+  for (int j = 0; j < 32; ++j) inv[j] = (float)(1.0 / __builtin_pow(1.0e7, (double)(2 * j) / 64.0));
+}
+
 // Head geometry of the lisa-rs full-attention layer (attention.metal:13-23).
 constexpr int QH = 24;         // query heads
 constexpr int KVH = 4;         // KV heads
@@ -54,16 +59,23 @@ __device__ __forceinline__ float load_in_bf16(const void* p, size_t i, int is_bf
   return round_bf16(reinterpret_cast<const float*>(p)[i]);
 }
 
-// RoPE inverse frequency 1/theta^(2j/64), theta = 1e7, evaluated in double and
-// rounded to f32; the angle is the reference's f32 product pos * inv_freq
-// (attention.metal:147); cos/sin of that f32 angle are evaluated in double.
-__device__ __forceinline__ void rope_cs(uint32_t pos, int j, float& c, float& s) {
-  const float inv = (float)(1.0 / pow(1.0e7, (double)(2 * j) / 64.0));
-  const float angle = (float)pos * inv;
+// RoPE: the reference's f32 angle pos * inv_freq[j] (attention.metal:147) with
+// inv_freq[j] = 1/theta^(2j/64), theta = 1e7, computed on the host in double
+// and rounded to f32; cos/sin of the f32 angle are evaluated in double and
+// rounded to f32 (host_rope_table computes the same values on the host).
+__device__ __forceinline__ void rope_cs(uint32_t pos, float inv_freq, float& c, float& s) {
+  const float angle = (float)pos * inv_freq;
   double sd, cd;
   sincos((double)angle, &sd, &cd);
   c = (float)cd;
   s = (float)sd;
+}
+
+// 2^x on the SFU (ex2.approx, about 2 ulp); used for softmax weights.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __device__ __forceinline__ uint64_t global_timer_ns() {
@@ -127,6 +139,12 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
+// Prefetch one tensor-map box into L2 (no shared memory, no completion).
+__device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap* map, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(map), "r"(c0), "r"(c1),
+               "r"(c2)
+               : "memory");
+}
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
@@ -157,6 +175,11 @@ __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
   uint32_t y;
   asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
   return y;
+}
+
+// bar.sync on a named barrier (ids 1..15) for a subset of the CTA's warps.
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 // Programmatic dependent launch.

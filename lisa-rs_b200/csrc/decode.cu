@@ -28,16 +28,11 @@
 #include "decode.cuh"
 
 #include <algorithm>
+#include <cmath>
 
 namespace lisa {
 
 namespace {
-
-struct TileCursor {
-  uint32_t chunk;   // chunk index
-  uint32_t tile;    // tile within chunk
-  uint32_t ntiles;  // tiles in this chunk
-};
 
 __device__ __forceinline__ uint32_t chunk_tiles(uint32_t chunk, uint32_t extent) {
   const uint32_t lo = chunk * DEC_CHUNK;
@@ -45,22 +40,15 @@ __device__ __forceinline__ uint32_t chunk_tiles(uint32_t chunk, uint32_t extent)
   return (n + DEC_TILE - 1) / DEC_TILE;
 }
 
-__device__ __forceinline__ void cursor_next(TileCursor& c, uint32_t stride, uint32_t extent, uint32_t nchunks) {
-  if (++c.tile == c.ntiles) {
-    c.tile = 0;
-    c.chunk += stride;
-    c.ntiles = c.chunk < nchunks ? chunk_tiles(c.chunk, extent) : 0;
-  }
-}
-
-// Issues the TMA loads of one 16-token tile (K and V, 4 boxes of 64 dims each).
+// Issues the TMA loads of one 64-token stage: K and V, 4 boxes of 64 dims
+// (128-byte swizzled rows) each.
 __device__ __forceinline__ void issue_tile(uint8_t* stage, uint64_t* full, const CUtensorMap* tk,
                                            const CUtensorMap* tv, uint32_t row0, int kvh) {
   mbar_arrive_expect_tx(full, DEC_STAGE_BYTES);
 #pragma unroll
   for (int st = 0; st < 4; ++st) {
-    tma_load_3d(stage + st * 2048, tk, full, st * 64, (int)row0, kvh);
-    tma_load_3d(stage + 8192 + st * 2048, tv, full, st * 64, (int)row0, kvh);
+    tma_load_3d(stage + st * (DEC_TILE * 128), tk, full, st * 64, (int)row0, kvh);
+    tma_load_3d(stage + DEC_STAGE_BYTES / 2 + st * (DEC_TILE * 128), tv, full, st * 64, (int)row0, kvh);
   }
 }
 
@@ -87,8 +75,7 @@ __device__ __forceinline__ void new_kv_row(const DecodeParams& p, int r, int kvh
     o[i] = n[i];
     if (lane < 8) {
       const int j = (lane & 3) * 8 + i;  // pair index 0..31
-      float c, s;
-      rope_cs(pos, j, c, s);
+      const float c = p.rope_c[r][j], s = p.rope_s[r][j];
       o[i] = lane < 4 ? n[i] * c - partner * s : n[i] * c + partner * s;
     }
   }
@@ -103,170 +90,216 @@ __device__ __forceinline__ void new_kv_row(const DecodeParams& p, int r, int kvh
 
 }  // namespace
 
-// One CTA = one kv head x a strided set of chunks; ROWS warps, warp m serves
-// query row m (6 heads). Thread 0 is also the TMA producer.
+// Per query row, in shared memory: stage maxima and sums per (warp, head) and
+// the warps' P^T fragments, double-buffered by stage parity.
+struct RowXch {
+  float red[2][4][8];
+  float lsum[2][4][8];
+  uint2 pb[2][4][32];
+};
+
+// CTA = one kv head x a strided set of chunks. ROWS query rows x 4 compute
+// warps + 1 TMA producer warp. Compute warp (m, w): row m, tokens 16w..16w+15
+// of each 64-token stage for Q.K^T, head dims 64w..64w+63 for P.V.
 template <int ROWS>
-__global__ void __launch_bounds__(32 * ROWS, DEC_CTAS_PER_SM)
+__global__ void __launch_bounds__(32 * (4 * ROWS + 1), 1)
     decode_split_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                         const DecodeParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + DEC_STAGES * DEC_STAGE_BYTES);
+  RowXch* xch = reinterpret_cast<RowXch*>(smem + DEC_STAGES * DEC_STAGE_BYTES);
+  // query rows in bf16 at DEC_QS_OFF: [ROWS][8 heads][256]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + DEC_STAGES * DEC_STAGE_BYTES + 3 * DEC_XCH_BYTES);
   uint64_t* empty = full + DEC_STAGES;
+  int* slot_code = reinterpret_cast<int*>(empty + DEC_STAGES);  // chunk << 8 | tile, or -1 = end
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, q = lane & 3;
   const int kvh = blockIdx.x & 3;
-  const uint32_t stride = gridDim.x >> 2;
-  const uint32_t first_chunk = blockIdx.x >> 2;
-  const int m = warp;  // query row of this warp
+  constexpr int NCOMPUTE = 4 * ROWS;
 
+#ifdef LISA_DECODE_TRACE
+  if (threadIdx.x == 0) p.trace[16 + blockIdx.x * 4 + 0] = global_timer_ns();
+#endif
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tk);
     tma_prefetch_desc(&tv);
     for (int s = 0; s < DEC_STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], ROWS);
+      mbar_init(&empty[s], NCOMPUTE);
     }
     fence_mbar_init();
   }
   __syncthreads();
+  // Everything above overlaps the previous kernel on the stream; nothing
+  // global is read before it has completed.
+  pdl_wait_primary();
   pdl_launch_dependents();
 
-  // Producer cursor (thread 0 only) runs DEC_STAGES-1 tiles ahead.
-  TileCursor pc{first_chunk, 0, first_chunk < p.nchunks ? chunk_tiles(first_chunk, p.extent) : 0};
-  uint32_t issued = 0;
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < DEC_STAGES - 1 && pc.ntiles; ++s) {
-      issue_tile(smem + (issued % DEC_STAGES) * DEC_STAGE_BYTES, &full[issued % DEC_STAGES], &tk, &tv,
-                 pc.chunk * DEC_CHUNK + pc.tile * DEC_TILE, kvh);
-      ++issued;
-      cursor_next(pc, stride, p.extent, p.nchunks);
+  if (warp == NCOMPUTE) {
+    // ---------------- TMA producer ----------------
+    // Start streaming only after the compute warps have their q values: loads
+    // issued behind a full ring of KV traffic would wait for all of it.
+    named_bar_sync(6, 32 * (NCOMPUTE + 1));
+    if (lane == 0) {
+      // Chunks of this kv head are taken dynamically (one atomic per chunk);
+      // a chunk's numerics do not depend on which CTA runs it.
+      uint32_t i = 0;
+      bool done = false;
+      while (!done) {
+        const uint32_t chunk = atomicAdd(&p.sched[kvh], 1u);
+        done = chunk >= p.nchunks;
+        const uint32_t nt = done ? 1 : chunk_tiles(chunk, p.extent);
+        for (uint32_t t = 0; t < nt; ++t, ++i) {
+          const uint32_t slot = i % DEC_STAGES;
+          if (i >= DEC_STAGES && !mbar_wait(&empty[slot], ((i / DEC_STAGES) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) {
+            done = true;
+            break;
+          }
+          slot_code[slot] = done ? -1 : (int)((chunk << 8) | t);
+          if (done) {
+            mbar_arrive(&full[slot]);  // end marker, no data
+            break;
+          }
+          issue_tile(smem + slot * DEC_STAGE_BYTES, &full[slot], &tk, &tv, chunk * DEC_CHUNK + t * DEC_TILE, kvh);
+        }
+      }
     }
+    return;
   }
 
-  // ---- query prologue: q RMSNorm + RoPE straight into B fragments ----------
-  // b0[kk] = Q[head g][16kk + 2q, +1], b1[kk] = Q[head g][16kk + 8 + 2q, +1].
+  const int m = warp >> 2, w = warp & 3;
+  RowXch& X = xch[m];
+
+  // ---- query prologue: q RMSNorm + RoPE (attention.metal:118-155) ----------
+  // Warp w normalises heads w and w+4 of row m (heads 6, 7 are zero padding)
+  // into shared memory, 8 dims per lane; then every warp loads its B
+  // fragments b0[kk] = Q[head g][16kk + 2q, +1], b1[kk] = Q[head g][16kk+8+2q, +1].
   uint32_t bq0[16], bq1[16];
   {
-    const uint32_t pos = p.base + m;
-    float x[64];
-    float ss = 0.f;
-    const int h = kvh * GQA + g;
-    const size_t qb = (size_t)m * QROW + (size_t)h * 512;
+    uint16_t* qs = reinterpret_cast<uint16_t*>(smem + DEC_QS_OFF) + m * (8 * HD);
+#pragma unroll 1
+    for (int hl = w; hl < 8; hl += 4) {
+      uint4 packed = make_uint4(0u, 0u, 0u, 0u);
+      if (hl < GQA) {
+        const size_t in = (size_t)m * QROW + (size_t)(kvh * GQA + hl) * 512 + lane * 8;
+        float x[8], ss = 0.f;
 #pragma unroll
-    for (int kk = 0; kk < 16; ++kk) {
+        for (int i = 0; i < 8; ++i) {
+          x[i] = load_in_bf16(p.q_gate, in + i, p.in_bf16);
+          ss += x[i] * x[i];
+        }
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int d = 16 * kk + 2 * q + (e & 1) + (e >> 1) * 8;
-        const float v = g < GQA ? load_in_bf16(p.q_gate, qb + d, p.in_bf16) : 0.f;
-        x[kk * 4 + e] = v;
-        ss += v * v;
+        for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        const float inv = 1.0f / sqrtf(ss / 256.0f + p.eps);
+        float o[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float n = x[i] * inv * bf16_bits_to_f32(p.q_norm_w[lane * 8 + i]);
+          const float partner = __shfl_xor_sync(0xffffffffu, n, 4);
+          o[i] = n;
+          if (lane < 8) {
+            const int j = (lane & 3) * 8 + i;  // pair index 0..31
+            const float c = p.rope_c[m][j], sn = p.rope_s[m][j];
+            o[i] = lane < 4 ? n * c - partner * sn : n * c + partner * sn;
+          }
+        }
+        packed = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
+                            pack_bf16x2(o[6], o[7]));
       }
+      *reinterpret_cast<uint4*>(qs + hl * HD + lane * 8) = packed;
     }
-    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-    const float inv = 1.0f / sqrtf(ss / 256.0f + p.eps);
+    named_bar_sync(6, 32 * (NCOMPUTE + 1));  // all q read: release the producer
+    const uint32_t qaddr = smem_u32(qs) + (lane & 7) * (HD * 2) + (lane >> 3) * 16;
 #pragma unroll
-    for (int kk = 0; kk < 16; ++kk)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int d = 16 * kk + 2 * q + (e & 1) + (e >> 1) * 8;
-        x[kk * 4 + e] = x[kk * 4 + e] * inv * bf16_bits_to_f32(p.q_norm_w[d]);
-      }
-    // pairs (d, d+32) for d < 32 live in (kk, kk+2) of the same lane
-#pragma unroll
-    for (int kk = 0; kk < 2; ++kk)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int d = 16 * kk + 2 * q + (e & 1) + (e >> 1) * 8;
-        float c, s;
-        rope_cs(pos, d, c, s);
-        const float a = x[kk * 4 + e], b = x[(kk + 2) * 4 + e];
-        x[kk * 4 + e] = a * c - b * s;
-        x[(kk + 2) * 4 + e] = b * c + a * s;
-      }
-#pragma unroll
-    for (int kk = 0; kk < 16; ++kk) {
-      bq0[kk] = g < GQA ? pack_bf16x2(x[kk * 4 + 0], x[kk * 4 + 1]) : 0u;
-      bq1[kk] = g < GQA ? pack_bf16x2(x[kk * 4 + 2], x[kk * 4 + 3]) : 0u;
-    }
+    for (int kp = 0; kp < 8; ++kp) ldmatrix_x4(qaddr + kp * 64, bq0[2 * kp], bq1[2 * kp], bq0[2 * kp + 1], bq1[2 * kp + 1]);
   }
 
   // Row m attends local rows [0, lim).
   const int64_t lim64 = (int64_t)p.base + m + 1 - (int64_t)p.kv_lo;
   const uint32_t lim = lim64 <= 0 ? 0u : (uint32_t)(lim64 < (int64_t)p.extent ? lim64 : (int64_t)p.extent);
 
-  float o[16][4];
+  float o[4][4];  // O^T for dims 64w + 16i + {g, g+8}, heads 2q, 2q+1
 #pragma unroll
-  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  for (int i = 0; i < 4; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // heads 2q, 2q+1
 
-  TileCursor cc{first_chunk, 0, first_chunk < p.nchunks ? chunk_tiles(first_chunk, p.extent) : 0};
-  uint32_t it = 0;
-  while (cc.ntiles) {
-    const int s = it % DEC_STAGES;
+#ifdef LISA_DECODE_TRACE
+  if (threadIdx.x == 0) p.trace[16 + blockIdx.x * 4 + 1] = global_timer_ns();
+  unsigned long long tr[8] = {};
+  long long tlast = clock64();
+#define DEC_TRACE(k)            \
+  {                             \
+    const long long tn = clock64(); \
+    tr[k] += tn - tlast;        \
+    tlast = tn;                 \
+  }
+#else
+#define DEC_TRACE(k)
+#endif
+  const int bar_row = 1 + m;  // named barrier of row m's 4 warps
+  for (uint32_t it = 0;; ++it) {
+    const int s = it % DEC_STAGES, par = it & 1;
     uint8_t* stage = smem + s * DEC_STAGE_BYTES;
-    // producer: refill the stage consumed in the previous iteration
-    if (threadIdx.x == 0 && pc.ntiles) {
-      const uint32_t slot = issued % DEC_STAGES;
-      if (issued >= DEC_STAGES &&
-          !mbar_wait(&empty[slot], ((issued / DEC_STAGES) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) {
-        pc.ntiles = 0;
-      } else {
-        issue_tile(smem + slot * DEC_STAGE_BYTES, &full[slot], &tk, &tv, pc.chunk * DEC_CHUNK + pc.tile * DEC_TILE,
-                   kvh);
-        ++issued;
-        cursor_next(pc, stride, p.extent, p.nchunks);
-      }
-    }
+    DEC_TRACE(0);
     if (!mbar_wait(&full[s], (it / DEC_STAGES) & 1, p.err, ERR_TIMEOUT_FULL)) return;
+    DEC_TRACE(1);
+    const int code = slot_code[s];
+    if (code < 0) break;
+    const uint32_t cur_chunk = (uint32_t)code >> 8, cur_tile = (uint32_t)code & 0xffu;
+    const uint32_t row0 = cur_chunk * DEC_CHUNK + cur_tile * DEC_TILE;
+    const uint32_t sK = smem_u32(stage), sV = sK + DEC_STAGE_BYTES / 2;
 
-    const uint32_t row0 = cc.chunk * DEC_CHUNK + cc.tile * DEC_TILE;
-    const uint32_t sK = smem_u32(stage), sV = sK + 8192;
-
-    // Substitute this call's new K/V rows (they are appended here).
-    {
-      bool wrote = false;
+    // This call's new K/V rows are appended here: warp (0, 0) normalises and
+    // ropes them, writes the cache and substitutes them in the staged tile.
+    bool has_new = false;
 #pragma unroll
-      for (int r = 0; r < ROWS; ++r) {
-        const int64_t lp = (int64_t)p.base + r - (int64_t)p.kv_lo;
-        if (lp >= (int64_t)row0 && lp < (int64_t)row0 + DEC_TILE && lp < (int64_t)p.extent) {
-          uint4 kr, vr;
-          new_kv_row(p, r, kvh, p.base + r, lane, kr, vr);
-          const uint32_t trow = (uint32_t)lp - row0;
-          const uint32_t off = (lane >> 3) * 2048 + swz128(trow, lane & 7);
-          *reinterpret_cast<uint4*>(stage + off) = kr;
-          *reinterpret_cast<uint4*>(stage + 8192 + off) = vr;
-          if (m == 0) {
+    for (int r = 0; r < ROWS; ++r) {
+      const int64_t lp = (int64_t)p.base + r - (int64_t)p.kv_lo;
+      has_new |= lp >= (int64_t)row0 && lp < (int64_t)row0 + DEC_TILE && lp < (int64_t)p.extent;
+    }
+    if (has_new) {
+      if (warp == 0) {
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r) {
+          const int64_t lp = (int64_t)p.base + r - (int64_t)p.kv_lo;
+          if (lp >= (int64_t)row0 && lp < (int64_t)row0 + DEC_TILE && lp < (int64_t)p.extent) {
+            uint4 kr, vr;
+            new_kv_row(p, r, kvh, p.base + r, lane, kr, vr);
+            const uint32_t off = (lane >> 3) * (DEC_TILE * 128) + swz128((uint32_t)lp - row0, lane & 7);
+            *reinterpret_cast<uint4*>(stage + off) = kr;
+            *reinterpret_cast<uint4*>(stage + DEC_STAGE_BYTES / 2 + off) = vr;
             const size_t go = ((size_t)kvh * p.window_rows + (size_t)lp) * HD + lane * 8;
             *reinterpret_cast<uint4*>(p.k_cache + go) = kr;
             *reinterpret_cast<uint4*>(p.v_cache + go) = vr;
           }
-          wrote = true;
         }
-      }
-      if (wrote) {
         fence_proxy_async_smem();
-        __syncwarp();
       }
+      named_bar_sync(5, 32 * NCOMPUTE);
     }
 
-    // S^T = K . Q^T
-    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+    // S^T[16 tok x 8 heads] = K[16w.., :] . Q^T, two independent mma chains
+    float sc[4] = {0.f, 0.f, 0.f, 0.f}, sd[4] = {0.f, 0.f, 0.f, 0.f};
     {
       const int mi = lane >> 3, rr = lane & 7;
-      const uint32_t tok = rr + (mi & 1) * 8;
+      const uint32_t tok = 16 * w + rr + (mi & 1) * 8;
 #pragma unroll
       for (int kk = 0; kk < 16; ++kk) {
         const uint32_t chunk = kk * 2 + (mi >> 1);
         uint32_t a0, a1, a2, a3;
-        ldmatrix_x4(sK + (chunk >> 3) * 2048 + swz128(tok, chunk & 7), a0, a1, a2, a3);
-        mma_bf16_16816(sc, a0, a1, a2, a3, bq0[kk], bq1[kk]);
+        ldmatrix_x4(sK + (chunk >> 3) * (DEC_TILE * 128) + swz128(tok, chunk & 7), a0, a1, a2, a3);
+        if (kk & 1)
+          mma_bf16_16816(sd, a0, a1, a2, a3, bq0[kk], bq1[kk]);
+        else
+          mma_bf16_16816(sc, a0, a1, a2, a3, bq0[kk], bq1[kk]);
       }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sc[e] += sd[e];
     }
-    // scale + causal mask: c0,c1 -> token row0+g, c2,c3 -> token row0+g+8
-    const bool v0 = row0 + g < lim, v1 = row0 + g + 8 < lim;
+    // scale + causal mask: c0,c1 -> token row0+16w+g, c2,c3 -> +8
+    const uint32_t t0 = row0 + 16 * w + g;
+    const bool v0 = t0 < lim, v1 = t0 + 8 < lim;
     sc[0] = v0 ? sc[0] * SCALE : -INFINITY;
     sc[1] = v0 ? sc[1] * SCALE : -INFINITY;
     sc[2] = v1 ? sc[2] * SCALE : -INFINITY;
@@ -277,62 +310,91 @@ __global__ void __launch_bounds__(32 * ROWS, DEC_CTAS_PER_SM)
       mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
       mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
     }
+    DEC_TRACE(2);
+    if (g == 0) *reinterpret_cast<float2*>(&X.red[par][w][2 * q]) = make_float2(mx0, mx1);
+    named_bar_sync(bar_row, 128);
+    DEC_TRACE(3);
+#pragma unroll
+    for (int ww = 0; ww < 4; ++ww) {
+      const float2 r2 = *reinterpret_cast<const float2*>(&X.red[par][ww][2 * q]);
+      mx0 = fmaxf(mx0, r2.x);
+      mx1 = fmaxf(mx1, r2.y);
+    }
     const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
-    const float al0 = n0 == -INFINITY ? 1.f : exp2f(LOG2E * (m0 - n0));
-    const float al1 = n1 == -INFINITY ? 1.f : exp2f(LOG2E * (m1 - n1));
-    const float p0 = n0 == -INFINITY ? 0.f : exp2f(LOG2E * (sc[0] - n0));
-    const float p1 = n1 == -INFINITY ? 0.f : exp2f(LOG2E * (sc[1] - n1));
-    const float p2 = n0 == -INFINITY ? 0.f : exp2f(LOG2E * (sc[2] - n0));
-    const float p3 = n1 == -INFINITY ? 0.f : exp2f(LOG2E * (sc[3] - n1));
+    const float al0 = n0 == -INFINITY ? 1.f : fast_exp2(LOG2E * (m0 - n0));
+    const float al1 = n1 == -INFINITY ? 1.f : fast_exp2(LOG2E * (m1 - n1));
+    const float p0 = n0 == -INFINITY ? 0.f : fast_exp2(LOG2E * (sc[0] - n0));
+    const float p1 = n1 == -INFINITY ? 0.f : fast_exp2(LOG2E * (sc[1] - n1));
+    const float p2 = n0 == -INFINITY ? 0.f : fast_exp2(LOG2E * (sc[2] - n0));
+    const float p3 = n1 == -INFINITY ? 0.f : fast_exp2(LOG2E * (sc[3] - n1));
     m0 = n0;
     m1 = n1;
     const uint32_t x0 = pack_bf16x2(p0, p1), x1 = pack_bf16x2(p2, p3);
     // the denominator sums the same bf16 weights the PV product uses
-    l0 = l0 * al0 + (bf16_bits_to_f32(x0 & 0xffffu) + bf16_bits_to_f32(x1 & 0xffffu));
-    l1 = l1 * al1 + (bf16_bits_to_f32(x0 >> 16) + bf16_bits_to_f32(x1 >> 16));
+    float ls0 = bf16_bits_to_f32(x0 & 0xffffu) + bf16_bits_to_f32(x1 & 0xffffu);
+    float ls1 = bf16_bits_to_f32(x0 >> 16) + bf16_bits_to_f32(x1 >> 16);
+#pragma unroll
+    for (int off = 4; off <= 16; off <<= 1) {
+      ls0 += __shfl_xor_sync(0xffffffffu, ls0, off);
+      ls1 += __shfl_xor_sync(0xffffffffu, ls1, off);
+    }
+    if (g == 0) *reinterpret_cast<float2*>(&X.lsum[par][w][2 * q]) = make_float2(ls0, ls1);
+    X.pb[par][w][lane] = make_uint2(movmatrix_trans(x0), movmatrix_trans(x1));
+    DEC_TRACE(4);
+    named_bar_sync(bar_row, 128);
+    DEC_TRACE(5);
+    {
+      float t0s = 0.f, t1s = 0.f;
+#pragma unroll
+      for (int ww = 0; ww < 4; ++ww) {
+        const float2 r2 = *reinterpret_cast<const float2*>(&X.lsum[par][ww][2 * q]);
+        t0s += r2.x;
+        t1s += r2.y;
+      }
+      l0 = l0 * al0 + t0s;
+      l1 = l1 * al1 + t1s;
+    }
     if (__any_sync(0xffffffffu, al0 != 1.f || al1 != 1.f)) {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
+      for (int i = 0; i < 4; ++i) {
         o[i][0] *= al0;
         o[i][1] *= al1;
         o[i][2] *= al0;
         o[i][3] *= al1;
       }
     }
-    const uint32_t b0 = movmatrix_trans(x0), b1 = movmatrix_trans(x1);
-    // O^T += V^T . P^T
+    // O^T[64w.., heads] += V^T . P^T over the stage's 64 tokens
     {
       const int mi = lane >> 3, rr = lane & 7;
-      const uint32_t tok = rr + (mi >> 1) * 8;
+      const uint32_t vbase = sV + w * (DEC_TILE * 128);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const uint32_t chunk = 2 * i + (mi & 1);
-        uint32_t a0, a1, a2, a3;
-        ldmatrix_x4_trans(sV + (chunk >> 3) * 2048 + swz128(tok, chunk & 7), a0, a1, a2, a3);
-        mma_bf16_16816(o[i], a0, a1, a2, a3, b0, b1);
+      for (int kk = 0; kk < 4; ++kk) {
+        const uint2 b = X.pb[par][kk][lane];
+        const uint32_t tok = 16 * kk + rr + (mi >> 1) * 8;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          uint32_t a0, a1, a2, a3;
+          ldmatrix_x4_trans(vbase + swz128(tok, 2 * i + (mi & 1)), a0, a1, a2, a3);
+          mma_bf16_16816(o[i], a0, a1, a2, a3, b.x, b.y);
+        }
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
+    DEC_TRACE(6);
 
-    if (cc.tile + 1 == cc.ntiles) {
+    if (cur_tile + 1 == chunk_tiles(cur_chunk, p.extent)) {
       // chunk done: write its partial
-      float t0 = l0, t1 = l1;
-#pragma unroll
-      for (int off = 4; off <= 16; off <<= 1) {
-        t0 += __shfl_xor_sync(0xffffffffu, t0, off);
-        t1 += __shfl_xor_sync(0xffffffffu, t1, off);
-      }
-      const size_t unit = ((size_t)m * KVH + kvh) * p.chunk_cap + cc.chunk;
-      if (g == 0) {
+      const size_t unit = ((size_t)m * KVH + kvh) * p.chunk_cap + cur_chunk;
+      if (w == 0 && g == 0) {
         float* ml = p.part_ml + unit * 16;
         *reinterpret_cast<float2*>(ml + 2 * q) = make_float2(m0, m1);
-        *reinterpret_cast<float2*>(ml + 8 + 2 * q) = make_float2(t0, t1);
+        *reinterpret_cast<float2*>(ml + 8 + 2 * q) = make_float2(l0, l1);
       }
       float* po = p.part_o + unit * 2048;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int d = 16 * i + g;
+      for (int i = 0; i < 4; ++i) {
+        const int d = 64 * w + 16 * i + g;
         *reinterpret_cast<float2*>(po + d * 8 + 2 * q) = make_float2(o[i][0], o[i][1]);
         *reinterpret_cast<float2*>(po + (d + 8) * 8 + 2 * q) = make_float2(o[i][2], o[i][3]);
         o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
@@ -340,22 +402,41 @@ __global__ void __launch_bounds__(32 * ROWS, DEC_CTAS_PER_SM)
       m0 = m1 = -INFINITY;
       l0 = l1 = 0.f;
     }
-    cursor_next(cc, stride, p.extent, p.nchunks);
-    ++it;
+    DEC_TRACE(7);
   }
+#ifdef LISA_DECODE_TRACE
+  if (lane == 0)
+    for (int k = 0; k < 8; ++k) atomicAdd(&p.trace[k], tr[k]);
+  if (lane == 0 && warp == 0) atomicAdd(&p.trace[8], 1ull);
+  if (threadIdx.x == 0) p.trace[16 + blockIdx.x * 4 + 2] = global_timer_ns();
+#endif
 }
 
-// Merges one row's chunk partials for one kv head and 8 dims, in a fixed
-// order that depends only on the row's own context (8 interleaved phases,
-// summed phase 0..7), then either applies the gate (gated_out) or writes the
-// window partial (win_o / win_ml). Grid: rows * 4 * 32 CTAs of 256 threads.
-// Thread: slot = tid & 31 -> (dim = db*8 + slot/4, heads 2*(slot&3), +1),
-// phase = tid >> 5 takes chunks c = phase, phase + 8, ...
-__global__ void __launch_bounds__(256) decode_combine_kernel(const DecodeParams p) {
+// Merges one row's chunk partials for one kv head and 8 dims. Thread
+// (phase, slot): slot = tid & 31 -> (dim = db*8 + slot/4, heads 2*(slot&3), +1);
+// phase = tid >> 5 folds chunks c = phase, phase + 32, ... with an online
+// log-sum-exp merge; the 32 phase states are then merged in phase order. The
+// order depends only on the row's own context, so verify rows stay
+// bit-identical to single-row decode. Applies the gate (gated_out) or writes
+// the window partial (win_o / win_ml). Grid rows * 4 * 32 CTAs of 1024 threads.
+struct Lse2 {
+  float m0, m1, a0, a1, d0, d1;  // max, weighted O, weighted sum for 2 heads
+};
+
+__device__ __forceinline__ void lse_fold(float& m, float& a, float& d, float cm, float ca, float cd) {
+  const float nm = fmaxf(m, cm);
+  if (nm == -INFINITY) return;
+  const float wo = fast_exp2(LOG2E * (m - nm)), wn = fast_exp2(LOG2E * (cm - nm));
+  a = a * wo + ca * wn;
+  d = d * wo + cd * wn;
+  m = nm;
+}
+
+__global__ void __launch_bounds__(CMB_THREADS) decode_combine_kernel(const DecodeParams p) {
   pdl_wait_primary();
-  __shared__ float2 s_acc[CMB_PHASES][32];
-  __shared__ float2 s_den[CMB_PHASES][32];
-  __shared__ float2 s_max[CMB_PHASES][32];
+  pdl_launch_dependents();
+  if (blockIdx.x == 0 && threadIdx.x < KVH) p.sched[threadIdx.x] = 0;  // ready for the next launch
+  __shared__ Lse2 s_state[CMB_PHASES][32];
   const int db = blockIdx.x & 31;
   const int kvh = (blockIdx.x >> 5) & 3;
   const int m = blockIdx.x >> 7;
@@ -368,52 +449,48 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(const DecodeParams 
   const uint32_t nch = (lim + DEC_CHUNK - 1) / DEC_CHUNK;
   const size_t unit0 = ((size_t)m * KVH + kvh) * p.chunk_cap;
 
-  // global max per head (exact in any order)
-  float2 mx = make_float2(-INFINITY, -INFINITY);
-  for (uint32_t c = phase; c < nch; c += CMB_PHASES) {
-    const float2 v = *reinterpret_cast<const float2*>(p.part_ml + (unit0 + c) * 16 + 2 * hp);
-    mx.x = fmaxf(mx.x, v.x);
-    mx.y = fmaxf(mx.y, v.y);
-  }
-  s_max[phase][slot] = mx;
-  __syncthreads();
-  float2 gm = make_float2(-INFINITY, -INFINITY);
+  Lse2 st = {-INFINITY, -INFINITY, 0.f, 0.f, 0.f, 0.f};
+  constexpr int U = 4;  // chunks whose loads are in flight together
+  for (uint32_t c0 = phase; c0 < nch; c0 += U * CMB_PHASES) {
+    float2 cm[U], cl[U], ov[U];
 #pragma unroll
-  for (int ph = 0; ph < CMB_PHASES; ++ph) {
-    gm.x = fmaxf(gm.x, s_max[ph][slot].x);
-    gm.y = fmaxf(gm.y, s_max[ph][slot].y);
+    for (int u = 0; u < U; ++u) {
+      const uint32_t c = c0 + u * CMB_PHASES;
+      if (c < nch) {
+        const float* ml = p.part_ml + (unit0 + c) * 16;
+        cm[u] = *reinterpret_cast<const float2*>(ml + 2 * hp);
+        cl[u] = *reinterpret_cast<const float2*>(ml + 8 + 2 * hp);
+        ov[u] = *reinterpret_cast<const float2*>(p.part_o + (unit0 + c) * 2048 + dim * 8 + 2 * hp);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (c0 + u * CMB_PHASES < nch) {
+        lse_fold(st.m0, st.a0, st.d0, cm[u].x, ov[u].x, cl[u].x);
+        lse_fold(st.m1, st.a1, st.d1, cm[u].y, ov[u].y, cl[u].y);
+      }
+    }
   }
-  float2 acc = make_float2(0.f, 0.f), den = make_float2(0.f, 0.f);
-  for (uint32_t c = phase; c < nch; c += CMB_PHASES) {
-    const float* ml = p.part_ml + (unit0 + c) * 16;
-    const float2 cm = *reinterpret_cast<const float2*>(ml + 2 * hp);
-    const float2 cl = *reinterpret_cast<const float2*>(ml + 8 + 2 * hp);
-    const float2 ov = *reinterpret_cast<const float2*>(p.part_o + (unit0 + c) * 2048 + dim * 8 + 2 * hp);
-    const float w0 = exp2f(LOG2E * (cm.x - gm.x)), w1 = exp2f(LOG2E * (cm.y - gm.y));
-    acc.x += w0 * ov.x;
-    acc.y += w1 * ov.y;
-    den.x += w0 * cl.x;
-    den.y += w1 * cl.y;
-  }
-  s_acc[phase][slot] = acc;
-  s_den[phase][slot] = den;
+  s_state[phase][slot] = st;
   __syncthreads();
+  // fixed binary tree over the 32 phase states
+#pragma unroll
+  for (int half = CMB_PHASES / 2; half >= 1; half >>= 1) {
+    if (phase < half) {
+      const Lse2 o = s_state[phase + half][slot];
+      lse_fold(st.m0, st.a0, st.d0, o.m0, o.a0, o.d0);
+      lse_fold(st.m1, st.a1, st.d1, o.m1, o.a1, o.d1);
+      s_state[phase][slot] = st;
+    }
+    __syncthreads();
+  }
   if (phase != 0) return;
-  acc = s_acc[0][slot];
-  den = s_den[0][slot];
-#pragma unroll
-  for (int ph = 1; ph < CMB_PHASES; ++ph) {
-    acc.x += s_acc[ph][slot].x;
-    acc.y += s_acc[ph][slot].y;
-    den.x += s_den[ph][slot].x;
-    den.y += s_den[ph][slot].y;
-  }
 #pragma unroll
   for (int e = 0; e < 2; ++e) {
     const int hl = 2 * hp + e;
     if (hl >= GQA) continue;
     const int h = kvh * GQA + hl;
-    const float a = e ? acc.y : acc.x, dn = e ? den.y : den.x, gmax = e ? gm.y : gm.x;
+    const float a = e ? st.a1 : st.a0, dn = e ? st.d1 : st.d0, gmax = e ? st.m1 : st.m0;
     const float o = nch ? a / dn : 0.f;
     if (p.gated_out) {
       // gate_out_bf16 (attention.metal:520-531); gate = bf16-rounded raw gate
@@ -463,13 +540,31 @@ static cudaError_t launch_split(const DecodeParams& p, const CUtensorMap& tk, co
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  const uint32_t per_head = std::min<uint32_t>(p.nchunks, (uint32_t)(num_sms * DEC_CTAS_PER_SM / KVH));
-  decode_split_kernel<ROWS><<<per_head * KVH, 32 * ROWS, DEC_SMEM_BYTES, stream>>>(tk, tv, p);
-  return cudaGetLastError();
+  const uint32_t per_head = std::min<uint32_t>(p.nchunks, (uint32_t)(num_sms / KVH));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(per_head * KVH);
+  cfg.blockDim = dim3(32 * (4 * ROWS + 1));
+  cfg.dynamicSmemBytes = DEC_SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, decode_split_kernel<ROWS>, tk, tv, p);
 }
 
-cudaError_t launch_decode(const DecodeParams& p, int rows, const CUtensorMap& tk, const CUtensorMap& tv,
+cudaError_t launch_decode(const DecodeParams& p_in, int rows, const CUtensorMap& tk, const CUtensorMap& tv,
                           int num_sms, cudaStream_t stream) {
+  DecodeParams p = p_in;
+  float inv[32];
+  host_inv_freq(inv);
+  for (int r = 0; r < 3; ++r)
+    for (int j = 0; j < 32; ++j) {
+      const float angle = (float)(p.base + (uint32_t)r) * inv[j];
+      p.rope_c[r][j] = (float)std::cos((double)angle);
+      p.rope_s[r][j] = (float)std::sin((double)angle);
+    }
   cudaError_t e;
   switch (rows) {
     case 1: e = launch_split<1>(p, tk, tv, num_sms, stream); break;
@@ -480,7 +575,7 @@ cudaError_t launch_decode(const DecodeParams& p, int rows, const CUtensorMap& tk
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(rows * KVH * (HD / CMB_DIMS_PER_CTA));
-  cfg.blockDim = dim3(256);
+  cfg.blockDim = dim3(CMB_THREADS);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];

@@ -7,17 +7,19 @@
 namespace lisa {
 
 // Split-KV geometry. A chunk is the unit of numerics: the online softmax runs
-// sequentially over the chunk's 16-token tiles and the chunk partials are
-// merged in a fixed order. Chunk boundaries depend only on the token index, so
-// a verify row gives bit-identical results to the same row decoded alone.
+// over the chunk's 64-token stages in order and the chunk partials are merged
+// in a fixed order. Chunk boundaries depend only on the token index, so a
+// verify row gives bit-identical results to the same row decoded alone.
 constexpr int DEC_CHUNK = 128;  // tokens per chunk
-constexpr int DEC_TILE = 16;    // tokens per pipeline stage (one mma M-tile)
+constexpr int DEC_TILE = 64;    // tokens per pipeline stage (4 warps x 16)
 constexpr int DEC_STAGES = 3;   // TMA ring depth per CTA
-constexpr int DEC_CTAS_PER_SM = 4;
-constexpr int DEC_STAGE_BYTES = 2 * DEC_TILE * 256 * 2;  // K + V tile, 16 KB
-constexpr int DEC_SMEM_BYTES = DEC_STAGES * DEC_STAGE_BYTES + 1024 + 256;
+constexpr int DEC_STAGE_BYTES = 2 * DEC_TILE * 256 * 2;  // K + V stage, 64 KB
+constexpr int DEC_XCH_BYTES = 2 * 4 * 8 * 4 * 2 + 2 * 4 * 32 * 8;  // per query row: max, sums, P fragments
+constexpr int DEC_QS_OFF = DEC_STAGES * DEC_STAGE_BYTES + 3 * DEC_XCH_BYTES + 256;  // after the mbarriers
+constexpr int DEC_SMEM_BYTES = DEC_QS_OFF + 3 * 8 * 256 * 2 + 1024;
 constexpr int CMB_DIMS_PER_CTA = 8;
-constexpr int CMB_PHASES = 8;
+constexpr int CMB_PHASES = 32;
+constexpr int CMB_THREADS = 32 * CMB_PHASES;
 
 struct DecodeParams {
   const void* q_gate;  // [rows][24][512]
@@ -38,10 +40,18 @@ struct DecodeParams {
   float* part_o;         // [rows][4][chunk_cap][256][8] unnormalised sums
   float* part_ml;        // [rows][4][chunk_cap][2][8]  {max, sum}
   int* err;
+  uint32_t* sched;       // [4] per-kv-head chunk counters: zero at launch, reset by the combine
+  // RoPE tables filled by launch_decode on the host: cos/sin of rows
+  // base..base+2 for the 32 rotated pairs.
+  float rope_c[3][32];
+  float rope_s[3][32];
   // combine outputs: gated bf16 [rows][6144] (final) or window partials
   uint16_t* gated_out;
   float* win_o;   // [rows][24][256]
   float* win_ml;  // [rows][24][2]
+#ifdef LISA_DECODE_TRACE
+  unsigned long long* trace;  // debug builds only: per-phase cycle totals
+#endif
 };
 
 // Launches the split-KV kernel and its combine (programmatic dependent launch)

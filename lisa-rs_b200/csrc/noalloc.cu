@@ -30,7 +30,7 @@ constexpr uint32_t NOALLOC_CHUNKS = (NOALLOC_MAX_POS + DEC_CHUNK - 1) / DEC_CHUN
 constexpr int NOALLOC_ROWS = 3;
 constexpr size_t NOALLOC_PO = (size_t)NOALLOC_ROWS * KVH * NOALLOC_CHUNKS * 2048;  // floats
 constexpr size_t NOALLOC_PM = (size_t)NOALLOC_ROWS * KVH * NOALLOC_CHUNKS * 16;    // floats
-constexpr size_t NOALLOC_FLOATS = NOALLOC_PO + NOALLOC_PM + 64;                   // + error word
+constexpr size_t NOALLOC_FLOATS = NOALLOC_PO + NOALLOC_PM + 64;  // + error word, chunk counters
 
 // The fixed scratch. In host code `g_noalloc_scratch` is only a stand-in
 // symbol, not a device address; the device address comes from
@@ -96,11 +96,12 @@ extern "C" int lisa_attn_decode_noalloc(void* k_cache, void* v_cache, uint32_t c
   p.part_o = scratch;
   p.part_ml = scratch + NOALLOC_PO;
   p.err = reinterpret_cast<int*>(scratch + NOALLOC_PO + NOALLOC_PM);
+  p.sched = reinterpret_cast<uint32_t*>(scratch + NOALLOC_PO + NOALLOC_PM + 16);
   p.gated_out = gated_out;
-  // Partials are fully written before they are read; only the error word must
-  // start at zero.
+  // Partials are fully written before they are read; the error word and the
+  // chunk counters must start at zero.
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (cudaMemsetAsync(p.err, 0, sizeof(int), st) != cudaSuccess) return LISA_ECUDA;
+  if (cudaMemsetAsync(p.err, 0, 128, st) != cudaSuccess) return LISA_ECUDA;
   CUtensorMap tk, tv;
   if (lisa_encode_kv_map(&tk, k_cache, p.extent, capacity, DEC_TILE, KVH) != LISA_OK ||
       lisa_encode_kv_map(&tv, v_cache, p.extent, capacity, DEC_TILE, KVH) != LISA_OK)

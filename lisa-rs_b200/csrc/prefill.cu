@@ -35,17 +35,28 @@ constexpr int PF_KV_BYTES = PF_BN * HD * 2;   // 32 KB
 constexpr int PF_P_BYTES = PF_BM * PF_BN * 2; // 16 KB
 constexpr int PF_OFF_K = PF_Q_BYTES;
 constexpr int PF_OFF_V = PF_OFF_K + 2 * PF_KV_BYTES;
-constexpr int PF_OFF_P = PF_OFF_V + 2 * PF_KV_BYTES;
-constexpr int PF_OFF_BAR = PF_OFF_P + PF_P_BYTES;
+constexpr int PF_OFF_P = PF_OFF_V + 2 * PF_KV_BYTES;  // two P buffers
+constexpr int PF_OFF_BAR = PF_OFF_P + 2 * PF_P_BYTES;
 constexpr int PF_SMEM_BYTES = PF_OFF_BAR + 256 + 1024;
-constexpr int PF_THREADS = 256;
+constexpr int PF_THREADS = 384;  // warp 0 TMA, warp 1 MMA, warps 4..11 softmax
 constexpr uint32_t PF_TMEM_COLS = 512;
 constexpr uint32_t PF_TMEM_O = 0;    // O accumulator: columns [0, 256)
 constexpr uint32_t PF_TMEM_S = 256;  // S buffers: columns [256, 320), [320, 384)
 constexpr float PF_RESCALE_LOG2 = 8.0f;
 
 // Barrier slots inside the barrier block.
-enum { B_Q = 0, B_KFULL = 1, B_VFULL = 3, B_EMPTY = 5, B_SFULL = 7, B_PFULL = 9, B_ODONE = 10, B_COUNT = 11 };
+// [2] = one per ring slot / buffer.
+enum {
+  B_Q = 0,
+  B_KFULL = 1,   // K tile landed
+  B_VFULL = 3,   // V tile landed
+  B_KEMPTY = 5,  // S MMA that read the K slot finished
+  B_VEMPTY = 7,  // PV MMA that read the V slot finished
+  B_SFULL = 9,   // S tile in TMEM
+  B_PFULL = 11,  // P tile in shared memory (128 softmax threads)
+  B_PVDONE = 13, // PV MMA that read the P buffer finished (O updated)
+  B_COUNT = 15
+};
 
 }  // namespace
 
@@ -80,7 +91,7 @@ __global__ void __launch_bounds__(256) prefill_prologue_kernel(const PrefillPara
     o[i] = n;
     if (lane < 8) {
       float c, s;
-      rope_cs(pos, (lane & 3) * 8 + i, c, s);
+      rope_cs(pos, p.inv_freq[(lane & 3) * 8 + i], c, s);
       o[i] = lane < 4 ? n * c - partner * s : n * c + partner * s;
     }
   }
@@ -96,6 +107,24 @@ __global__ void __launch_bounds__(256) prefill_prologue_kernel(const PrefillPara
     for (int i = 0; i < 8; ++i) v[i] = load_in_bf16(p.v_in, in + i, p.in_bf16);
     *reinterpret_cast<uint4*>(p.v_cache + out) =
         make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+  }
+}
+
+// Eight consecutive inputs rounded to bf16, vectorised (idx multiple of 8).
+__device__ __forceinline__ void load8_bf16(const void* src, size_t idx, int is_bf16, float (&out)[8]) {
+  if (is_bf16) {
+    const uint4 w = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(src) + idx);
+    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      out[2 * i] = bf16_bits_to_f32(u[i] & 0xffffu);
+      out[2 * i + 1] = bf16_bits_to_f32(u[i] >> 16);
+    }
+  } else {
+    const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(src) + idx);
+    const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(src) + idx + 4);
+    out[0] = round_bf16(a.x); out[1] = round_bf16(a.y); out[2] = round_bf16(a.z); out[3] = round_bf16(a.w);
+    out[4] = round_bf16(b.x); out[5] = round_bf16(b.y); out[6] = round_bf16(b.z); out[7] = round_bf16(b.w);
   }
 }
 
@@ -121,15 +150,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     tma_prefetch_desc(&tq);
     tma_prefetch_desc(&tk);
     tma_prefetch_desc(&tv);
-    mbar_init(&bars[B_Q], 1);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&bars[B_KFULL + s], 1);
-      mbar_init(&bars[B_VFULL + s], 1);
-      mbar_init(&bars[B_EMPTY + s], 1);
-      mbar_init(&bars[B_SFULL + s], 1);
-    }
-    mbar_init(&bars[B_PFULL], 128);
-    mbar_init(&bars[B_ODONE], 1);
+    for (int b = 0; b < B_COUNT; ++b) mbar_init(&bars[b], (b == B_PFULL || b == B_PFULL + 1) ? 256 : 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -142,19 +163,23 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
+    // ---------------- TMA producer, in the order the MMAs need the tiles:
+    // Q, K0, K1, V0, K2, V1, ... ----------------
     if (lane == 0) {
       mbar_arrive_expect_tx(&bars[B_Q], PF_Q_BYTES);
       for (int st = 0; st < 4; ++st) tma_load_3d(smem + st * (PF_BM * 128), &tq, &bars[B_Q], st * 64, r0, h);
-      for (int j = 0; j < n_tiles; ++j) {
+      auto load = [&](const CUtensorMap* map, int off, int full, int empty, int j) -> bool {
         const int s = j & 1;
-        if (j >= 2 && !mbar_wait(&bars[B_EMPTY + s], ((j >> 1) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) break;
-        uint8_t* ks = smem + PF_OFF_K + s * PF_KV_BYTES;
-        uint8_t* vs = smem + PF_OFF_V + s * PF_KV_BYTES;
-        mbar_arrive_expect_tx(&bars[B_KFULL + s], PF_KV_BYTES);
-        for (int st = 0; st < 4; ++st) tma_load_3d(ks + st * 8192, &tk, &bars[B_KFULL + s], st * 64, j * PF_BN, kvh);
-        mbar_arrive_expect_tx(&bars[B_VFULL + s], PF_KV_BYTES);
-        for (int st = 0; st < 4; ++st) tma_load_3d(vs + st * 8192, &tv, &bars[B_VFULL + s], st * 64, j * PF_BN, kvh);
+        if (j >= 2 && !mbar_wait(&bars[empty + s], ((j >> 1) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) return false;
+        uint8_t* dst = smem + off + s * PF_KV_BYTES;
+        mbar_arrive_expect_tx(&bars[full + s], PF_KV_BYTES);
+        for (int st = 0; st < 4; ++st) tma_load_3d(dst + st * 8192, map, &bars[full + s], st * 64, j * PF_BN, kvh);
+        return true;
+      };
+      bool ok = load(&tk, PF_OFF_K, B_KFULL, B_KEMPTY, 0);
+      for (int i = 1; ok && i <= n_tiles; ++i) {
+        if (i < n_tiles) ok = load(&tk, PF_OFF_K, B_KFULL, B_KEMPTY, i);
+        if (ok) ok = load(&tv, PF_OFF_V, B_VFULL, B_VEMPTY, i - 1);
       }
     }
     return;
@@ -180,16 +205,17 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
           umma_bf16(d, a, b, IDESC_S, kk > 0);
         }
         umma_commit(&bars[B_SFULL + s]);
+        umma_commit(&bars[B_KEMPTY + s]);
         return true;
       };
       if (ok) ok = issue_s(0);
       for (int j = 0; ok && j < n_tiles; ++j) {
         const int s = j & 1;
         if (j + 1 < n_tiles && !issue_s(j + 1)) break;
-        if (!mbar_wait(&bars[B_PFULL], j & 1, p.err, ERR_TIMEOUT_MMA)) break;
+        if (!mbar_wait(&bars[B_PFULL + s], (j >> 1) & 1, p.err, ERR_TIMEOUT_MMA)) break;
         if (!mbar_wait(&bars[B_VFULL + s], (j >> 1) & 1, p.err, ERR_TIMEOUT_FULL)) break;
         tc_fence_after();
-        const uint32_t sP = smem_u32(smem + PF_OFF_P);
+        const uint32_t sP = smem_u32(smem + PF_OFF_P + s * PF_P_BYTES);
         const uint32_t sV = smem_u32(smem + PF_OFF_V + s * PF_KV_BYTES);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
@@ -197,12 +223,12 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
           const uint64_t b = umma_desc_sw128(sV + kk * 2048, 8192, 1024);
           umma_bf16(tmem + PF_TMEM_O, a, b, IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&bars[B_ODONE]);
-        umma_commit(&bars[B_EMPTY + s]);
+        umma_commit(&bars[B_PVDONE + s]);
+        umma_commit(&bars[B_VEMPTY + s]);
       }
     }
     __syncwarp();
-    named_bar_sync(1, 160);
+    named_bar_sync(1, 288);
     tc_fence_after();
     tmem_dealloc(tmem, PF_TMEM_COLS);
     return;
@@ -210,13 +236,16 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 
   if (warp < 4) return;
 
-  // ---------------- softmax / correction / epilogue (warps 4..7) ----------------
-  const int wi = warp - 4;
+  // ---------------- softmax / correction / epilogue (warps 4..11) ----------------
+  // Warp 4+w and warp 8+w share TMEM lanes 32w..32w+31 (one query row per
+  // thread); both take the row max over all 64 scores of a tile, and each
+  // exponentiates, rescales and stores one half of the columns.
+  const int wi = (warp - 4) & 3;
+  const int half = (warp - 4) >> 2;
   const int row = wi * 32 + lane;  // row within the tile == TMEM lane
   const uint32_t lane_addr = tmem + ((uint32_t)(wi * 32) << 16);
   const uint32_t pos_row = p.base + (uint32_t)(r0 + row);
-  uint8_t* sP = smem + PF_OFF_P;
-  float m2 = -INFINITY, l = 0.f;
+  float m2 = -INFINITY, l = 0.f;  // running max (log2 domain), this half's sum
   bool ok = true;
   for (int j = 0; j < n_tiles; ++j) {
     const int b = j & 1;
@@ -230,96 +259,127 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     tmem_ld32(lane_addr + PF_TMEM_S + b * PF_BN + 32, sb);
     tmem_wait_ld();
     const uint32_t key0 = (uint32_t)j * PF_BN;
+    const bool full_tile = key0 + PF_BN - 1 <= pos_row;
     float s2[64];
-    float tmax = -INFINITY;
 #pragma unroll
     for (int c = 0; c < 64; ++c) {
       const float raw = __uint_as_float(c < 32 ? sa[c] : sb[c - 32]);
-      s2[c] = key0 + c <= pos_row ? raw * (SCALE * LOG2E) : -INFINITY;
-      tmax = fmaxf(tmax, s2[c]);
+      s2[c] = (full_tile || key0 + c <= pos_row) ? raw * (SCALE * LOG2E) : -INFINITY;
     }
-    const float mnew = fmaxf(m2, tmax);
+    float t[32];
+#pragma unroll
+    for (int c = 0; c < 32; ++c) t[c] = fmaxf(s2[c], s2[c + 32]);
+#pragma unroll
+    for (int w = 16; w >= 1; w >>= 1)
+#pragma unroll
+      for (int c = 0; c < w; ++c) t[c] = fmaxf(t[c], t[c + w]);
+    const float mnew = fmaxf(m2, t[0]);
     const bool need = mnew > m2 + PF_RESCALE_LOG2;  // also true for the first finite max
     float alpha = 1.f;
     if (need) {
-      alpha = exp2f(m2 - mnew);
+      alpha = fast_exp2(m2 - mnew);
       m2 = mnew;
     }
-    uint32_t pk[32];
-    float psum = 0.f;
+    uint32_t pk[16];
+    float ps[16];
 #pragma unroll
-    for (int c = 0; c < 32; ++c) {
-      const float e0 = m2 == -INFINITY ? 0.f : exp2f(s2[2 * c] - m2);
-      const float e1 = m2 == -INFINITY ? 0.f : exp2f(s2[2 * c + 1] - m2);
+    for (int c = 0; c < 16; ++c) {
+      const float x0 = half ? s2[32 + 2 * c] : s2[2 * c];
+      const float x1 = half ? s2[33 + 2 * c] : s2[2 * c + 1];
+      const float e0 = fast_exp2(x0 - m2);
+      const float e1 = fast_exp2(x1 - m2);
       pk[c] = pack_bf16x2(e0, e1);
-      psum += bf16_bits_to_f32(pk[c] & 0xffffu) + bf16_bits_to_f32(pk[c] >> 16);
+      ps[c] = bf16_bits_to_f32(pk[c] & 0xffffu) + bf16_bits_to_f32(pk[c] >> 16);
     }
-    l = l * alpha + psum;
-    if (j > 0) {
-      if (!mbar_wait(&bars[B_ODONE], (j - 1) & 1, p.err, ERR_TIMEOUT_MMA)) {
+#pragma unroll
+    for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+      for (int c = 0; c < w; ++c) ps[c] += ps[c + w];
+    l = l * alpha + ps[0];
+    if (j > 0 && __any_sync(0xffffffffu, need)) {
+      // O must hold exactly tiles < j before it is rescaled
+      if (!mbar_wait(&bars[B_PVDONE + (b ^ 1)], ((j - 1) >> 1) & 1, p.err, ERR_TIMEOUT_MMA)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      if (__any_sync(0xffffffffu, need)) {
 #pragma unroll 1
-        for (int c = 0; c < HD / 32; ++c) {
-          uint32_t ov[32];
-          tmem_ld32(lane_addr + PF_TMEM_O + c * 32, ov);
-          tmem_wait_ld();
+      for (int c = 0; c < HD / 64; ++c) {
+        const uint32_t col = PF_TMEM_O + half * (HD / 2) + c * 32;
+        uint32_t ov[32];
+        tmem_ld32(lane_addr + col, ov);
+        tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
-          tmem_st32(lane_addr + PF_TMEM_O + c * 32, ov);
-        }
-        tmem_wait_st();
+        for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+        tmem_st32(lane_addr + col, ov);
       }
+      tmem_wait_st();
     }
-    // P row -> shared memory, K-major 128-byte-swizzled rows of 64 keys
+    if (j >= 2 && !mbar_wait(&bars[B_PVDONE + b], ((j - 2) >> 1) & 1, p.err, ERR_TIMEOUT_MMA)) {
+      ok = false;  // P buffer b is free once PV_{j-2} finished
+      break;
+    }
+    uint8_t* sP = smem + PF_OFF_P + b * PF_P_BYTES;
 #pragma unroll
-    for (int c = 0; c < 8; ++c)
-      *reinterpret_cast<uint4*>(sP + swz128((uint32_t)row, (uint32_t)c)) =
+    for (int c = 0; c < 4; ++c)
+      *reinterpret_cast<uint4*>(sP + swz128((uint32_t)row, (uint32_t)(half * 4 + c))) =
           make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
     fence_proxy_async_smem();
     tc_fence_before();
-    mbar_arrive(&bars[B_PFULL]);
+    mbar_arrive(&bars[B_PFULL + b]);
   }
-  if (ok && mbar_wait(&bars[B_ODONE], (n_tiles - 1) & 1, p.err, ERR_TIMEOUT_MMA)) {
+  const int last = n_tiles - 1;
+  ok = ok && mbar_wait(&bars[B_PVDONE + (last & 1)], (last >> 1) & 1, p.err, ERR_TIMEOUT_MMA);
+  // Sum the two halves' denominators (half 0 + half 1) through the now idle
+  // P buffers.
+  float* lx = reinterpret_cast<float*>(smem + PF_OFF_P);
+  lx[half * PF_BM + row] = l;
+  named_bar_sync(2 + wi, 64);
+  const float l_row = lx[row] + lx[PF_BM + row];
+  if (ok) {
     tc_fence_after();
     const int r = r0 + row;
-    const float inv_l = 1.0f / l;
+    const float inv_l = 1.0f / l_row;
+    const size_t gbase = (size_t)r * QROW + (size_t)h * 512 + 256;
 #pragma unroll 1
-    for (int c = 0; c < HD / 32; ++c) {
+    for (int c = 0; c < HD / 64; ++c) {
+      const int col = half * (HD / 2) + c * 32;
       uint32_t ov[32];
-      tmem_ld32(lane_addr + PF_TMEM_O + c * 32, ov);
+      tmem_ld32(lane_addr + PF_TMEM_O + col, ov);
       tmem_wait_ld();
       if (r < p.rows) {
         uint32_t outw[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float y[2];
+        for (int g8 = 0; g8 < 4; ++g8) {
+          float gv[8];
+          load8_bf16(p.q_gate, gbase + col + g8 * 8, p.in_bf16, gv);
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int d = c * 32 + 2 * i + e;
-            const float gv = load_in_bf16(p.q_gate, (size_t)r * QROW + (size_t)h * 512 + 256 + d, p.in_bf16);
-            const float sg = 1.0f / (1.0f + exp2f(-LOG2E * gv));
-            y[e] = __uint_as_float(ov[2 * i + e]) * inv_l * sg;
+          for (int i = 0; i < 4; ++i) {
+            float y[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const float sg = 1.0f / (1.0f + exp2f(-LOG2E * gv[2 * i + e]));
+              y[e] = __uint_as_float(ov[g8 * 8 + 2 * i + e]) * inv_l * sg;
+            }
+            outw[g8 * 4 + i] = pack_bf16x2(y[0], y[1]);
           }
-          outw[i] = pack_bf16x2(y[0], y[1]);
         }
-        uint4* dst = reinterpret_cast<uint4*>(p.gated_out + (size_t)r * OROW + h * HD + c * 32);
+        uint4* dst = reinterpret_cast<uint4*>(p.gated_out + (size_t)r * OROW + h * HD + col);
 #pragma unroll
         for (int i = 0; i < 4; ++i) dst[i] = make_uint4(outw[4 * i], outw[4 * i + 1], outw[4 * i + 2], outw[4 * i + 3]);
       }
     }
   }
   tc_fence_before();
-  named_bar_sync(1, 160);
+  named_bar_sync(1, 288);
 }
 
 size_t prefill_workspace_bytes() { return (size_t)QH * PF_MAX_ROWS * HD * sizeof(uint16_t); }
 
-cudaError_t launch_prefill(const PrefillParams& p, int num_sms, cudaStream_t stream) {
+cudaError_t launch_prefill(const PrefillParams& p_in, int num_sms, cudaStream_t stream) {
   (void)num_sms;
+  PrefillParams p = p_in;
+  host_inv_freq(p.inv_freq);
   const int items = p.rows * (QH + KVH);
   prefill_prologue_kernel<<<(items + 7) / 8, 256, 0, stream>>>(p);
   cudaError_t e = cudaGetLastError();

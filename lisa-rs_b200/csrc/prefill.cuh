@@ -30,6 +30,7 @@ struct PrefillParams {
   uint16_t* q_ws;     // workspace: normalised query, bf16 [24][512][256]
   uint16_t* gated_out;  // [rows][6144]
   int* err;
+  float inv_freq[32];  // filled by launch_prefill
 };
 
 // Bytes of device workspace launch_prefill needs.

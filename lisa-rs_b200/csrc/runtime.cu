@@ -35,6 +35,7 @@ struct lisa_attn_ctx {
   void* prefill_ws = nullptr;  // prefill scratch
   size_t prefill_ws_bytes = 0;
   int* err = nullptr;
+  uint32_t* sched = nullptr;  // decode chunk counters [4]
   int num_sms = 148;
   uint32_t position = 0;
   bool verify_pending = false;
@@ -102,7 +103,7 @@ struct DeviceGuard {
 int run_decode(uint16_t* kc, uint16_t* vc, uint32_t window_rows, uint32_t kv_lo, uint32_t base, int rows,
                int in_dtype, const void* q_gate, const void* k, const void* v, const uint16_t* qn,
                const uint16_t* kn, float eps, float* part_o, float* part_ml, uint32_t chunk_cap, int* err,
-               uint16_t* gated, float* win_o, float* win_ml, int num_sms, cudaStream_t stream) {
+               uint32_t* sched, uint16_t* gated, float* win_o, float* win_ml, int num_sms, cudaStream_t stream) {
   DecodeParams p = {};
   p.q_gate = q_gate;
   p.k_in = k;
@@ -123,6 +124,7 @@ int run_decode(uint16_t* kc, uint16_t* vc, uint32_t window_rows, uint32_t kv_lo,
   p.part_o = part_o;
   p.part_ml = part_ml;
   p.err = err;
+  p.sched = sched;
   p.gated_out = gated;
   p.win_o = win_o;
   p.win_ml = win_ml;
@@ -165,9 +167,10 @@ int lisa_attn_create(int device, int n_layers, uint32_t capacity, lisa_attn_ctx*
   bool ok = cudaMalloc(&c->k, cache_bytes) == cudaSuccess && cudaMalloc(&c->v, cache_bytes) == cudaSuccess &&
             cudaMalloc(&c->part_o, po) == cudaSuccess && cudaMalloc(&c->part_ml, pm) == cudaSuccess &&
             cudaMalloc(&c->prefill_ws, c->prefill_ws_bytes) == cudaSuccess &&
-            cudaMalloc(&c->err, sizeof(int)) == cudaSuccess;
+            cudaMalloc(&c->err, sizeof(int)) == cudaSuccess && cudaMalloc(&c->sched, 64) == cudaSuccess;
   ok = ok && cudaMemset(c->k, 0, cache_bytes) == cudaSuccess && cudaMemset(c->v, 0, cache_bytes) == cudaSuccess &&
-       cudaMemset(c->err, 0, sizeof(int)) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;
+       cudaMemset(c->err, 0, sizeof(int)) == cudaSuccess && cudaMemset(c->sched, 0, 64) == cudaSuccess &&
+       cudaDeviceSynchronize() == cudaSuccess;
   if (!ok) {
     lisa_attn_destroy(c);
     return LISA_ECUDA;
@@ -185,6 +188,7 @@ int lisa_attn_destroy(lisa_attn_ctx* c) {
   cudaFree(c->part_ml);
   cudaFree(c->prefill_ws);
   cudaFree(c->err);
+  cudaFree(c->sched);
   delete c;
   return LISA_OK;
 }
@@ -209,7 +213,7 @@ int lisa_attn_decode(lisa_attn_ctx* c, int layer, uint32_t base, int rows, int i
   DeviceGuard guard(c->device);
   const size_t off = (size_t)layer * layer_elems(c);
   return run_decode(c->k + off, c->v + off, c->capacity, 0, base, rows, in_dtype, q_gate, k, v, qn, kn, eps,
-                    c->part_o, c->part_ml, c->chunk_cap, c->err, gated_out, nullptr, nullptr, c->num_sms,
+                    c->part_o, c->part_ml, c->chunk_cap, c->err, c->sched, gated_out, nullptr, nullptr, c->num_sms,
                     (cudaStream_t)stream);
 }
 
@@ -367,11 +371,14 @@ int lisa_attn_decode_window(void* k_cache, void* v_cache, uint32_t window_rows, 
   float* wo = reinterpret_cast<float*>(ws);
   float* wm = reinterpret_cast<float*>(ws + ((po + 255) & ~size_t(255)));
   int* err = reinterpret_cast<int*>(ws + ((po + 255) & ~size_t(255)) + ((pm + 255) & ~size_t(255)));
+  uint32_t* sched = reinterpret_cast<uint32_t*>(err + 16);
+  // error word and chunk counters start at zero
+  if (cudaMemsetAsync(err, 0, 128, (cudaStream_t)stream) != cudaSuccess) return LISA_ECUDA;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   return run_decode((uint16_t*)k_cache, (uint16_t*)v_cache, window_rows, kv_lo, base, rows, in_dtype, q_gate, k, v,
-                    qn, kn, eps, wo, wm, chunks, err, nullptr, part_o, part_ml, sms, (cudaStream_t)stream);
+                    qn, kn, eps, wo, wm, chunks, err, sched, nullptr, part_o, part_ml, sms, (cudaStream_t)stream);
 }
 
 int lisa_attn_merge_windows(int n_parts, int rows, const float* part_o, const float* part_ml, int in_dtype,
