@@ -111,7 +111,8 @@ __global__ void __launch_bounds__(32 * (4 * ROWS + 1), 1)
   // query rows in bf16 at DEC_QS_OFF: [ROWS][8 heads][256]
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + DEC_STAGES * DEC_STAGE_BYTES + 3 * DEC_XCH_BYTES);
   uint64_t* empty = full + DEC_STAGES;
-  int* slot_code = reinterpret_cast<int*>(empty + DEC_STAGES);  // chunk << 8 | tile, or -1 = end
+  uint64_t* qbar = empty + DEC_STAGES;                               // raw q + gains landed
+  int* slot_code = reinterpret_cast<int*>(qbar + 1);                 // chunk << 8 | tile, or -1 = end
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, q = lane & 3;
@@ -128,6 +129,7 @@ __global__ void __launch_bounds__(32 * (4 * ROWS + 1), 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], NCOMPUTE);
     }
+    mbar_init(qbar, 1);
     fence_mbar_init();
   }
   __syncthreads();
@@ -138,10 +140,17 @@ __global__ void __launch_bounds__(32 * (4 * ROWS + 1), 1)
 
   if (warp == NCOMPUTE) {
     // ---------------- TMA producer ----------------
-    // Start streaming only after the compute warps have their q values: loads
-    // issued behind a full ring of KV traffic would wait for all of it.
-    named_bar_sync(6, 32 * (NCOMPUTE + 1));
     if (lane == 0) {
+      // The query rows go first, so they are not queued behind the KV ring.
+      const uint32_t hb = p.in_bf16 ? 512u : 1024u;  // bytes of one head's 256 query values
+      mbar_arrive_expect_tx(qbar, ROWS * GQA * hb + 512);
+      for (int r = 0; r < ROWS; ++r)
+        for (int hl = 0; hl < GQA; ++hl) {
+          const size_t el = (size_t)r * QROW + (size_t)(kvh * GQA + hl) * 512;
+          const uint8_t* src = reinterpret_cast<const uint8_t*>(p.q_gate) + el * (p.in_bf16 ? 2 : 4);
+          bulk_load(smem + DEC_QS_OFF + r * DEC_QROW_BYTES + hl * hb, src, hb, qbar);
+        }
+      bulk_load(smem + DEC_WN_OFF, p.q_norm_w, 512, qbar);
       // Chunks of this kv head are taken dynamically (one atomic per chunk);
       // a chunk's numerics do not depend on which CTA runs it.
       uint32_t i = 0;
@@ -172,30 +181,45 @@ __global__ void __launch_bounds__(32 * (4 * ROWS + 1), 1)
   RowXch& X = xch[m];
 
   // ---- query prologue: q RMSNorm + RoPE (attention.metal:118-155) ----------
-  // Warp w normalises heads w and w+4 of row m (heads 6, 7 are zero padding)
-  // into shared memory, 8 dims per lane; then every warp loads its B
+  // The raw query of row m (6 heads) is in shared memory. Warp w normalises
+  // heads w and w+4 (heads 6, 7 are zero padding), 8 dims per lane, and writes
+  // bf16 rows [8][256] over the raw data; then every warp loads its B
   // fragments b0[kk] = Q[head g][16kk + 2q, +1], b1[kk] = Q[head g][16kk+8+2q, +1].
   uint32_t bq0[16], bq1[16];
   {
-    uint16_t* qs = reinterpret_cast<uint16_t*>(smem + DEC_QS_OFF) + m * (8 * HD);
-#pragma unroll 1
-    for (int hl = w; hl < 8; hl += 4) {
-      uint4 packed = make_uint4(0u, 0u, 0u, 0u);
-      if (hl < GQA) {
-        const size_t in = (size_t)m * QROW + (size_t)(kvh * GQA + hl) * 512 + lane * 8;
-        float x[8], ss = 0.f;
+    uint8_t* qrow = smem + DEC_QS_OFF + m * DEC_QROW_BYTES;
+    const uint16_t* wn = reinterpret_cast<const uint16_t*>(smem + DEC_WN_OFF);
+    if (!mbar_wait(qbar, 0, p.err, ERR_TIMEOUT_FULL)) return;
+    uint4 packed[2];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          x[i] = load_in_bf16(p.q_gate, in + i, p.in_bf16);
-          ss += x[i] * x[i];
+    for (int u = 0; u < 2; ++u) {
+      const int hl = w + 4 * u;
+      packed[u] = make_uint4(0u, 0u, 0u, 0u);
+      if (hl < GQA) {
+        float x[8], ss = 0.f;
+        if (p.in_bf16) {
+          const uint4 raw = *reinterpret_cast<const uint4*>(qrow + hl * 512 + lane * 16);
+          const uint32_t wds[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            x[2 * i] = bf16_bits_to_f32(wds[i] & 0xffffu);
+            x[2 * i + 1] = bf16_bits_to_f32(wds[i] >> 16);
+          }
+        } else {
+          const float4 a = *reinterpret_cast<const float4*>(qrow + hl * 1024 + lane * 32);
+          const float4 b = *reinterpret_cast<const float4*>(qrow + hl * 1024 + lane * 32 + 16);
+          x[0] = round_bf16(a.x); x[1] = round_bf16(a.y); x[2] = round_bf16(a.z); x[3] = round_bf16(a.w);
+          x[4] = round_bf16(b.x); x[5] = round_bf16(b.y); x[6] = round_bf16(b.z); x[7] = round_bf16(b.w);
         }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
 #pragma unroll
         for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
         const float inv = 1.0f / sqrtf(ss / 256.0f + p.eps);
         float o[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const float n = x[i] * inv * bf16_bits_to_f32(p.q_norm_w[lane * 8 + i]);
+          const float n = x[i] * inv * bf16_bits_to_f32(wn[lane * 8 + i]);
           const float partner = __shfl_xor_sync(0xffffffffu, n, 4);
           o[i] = n;
           if (lane < 8) {
@@ -204,12 +228,15 @@ __global__ void __launch_bounds__(32 * (4 * ROWS + 1), 1)
             o[i] = lane < 4 ? n * c - partner * sn : n * c + partner * sn;
           }
         }
-        packed = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
-                            pack_bf16x2(o[6], o[7]));
+        packed[u] = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
+                               pack_bf16x2(o[6], o[7]));
       }
-      *reinterpret_cast<uint4*>(qs + hl * HD + lane * 8) = packed;
     }
-    named_bar_sync(6, 32 * (NCOMPUTE + 1));  // all q read: release the producer
+    named_bar_sync(1 + m, 128);  // every raw value of row m has been read
+    uint16_t* qs = reinterpret_cast<uint16_t*>(qrow);
+#pragma unroll
+    for (int u = 0; u < 2; ++u) *reinterpret_cast<uint4*>(qs + (w + 4 * u) * HD + lane * 8) = packed[u];
+    named_bar_sync(1 + m, 128);
     const uint32_t qaddr = smem_u32(qs) + (lane & 7) * (HD * 2) + (lane >> 3) * 16;
 #pragma unroll
     for (int kp = 0; kp < 8; ++kp) ldmatrix_x4(qaddr + kp * 64, bq0[2 * kp], bq1[2 * kp], bq0[2 * kp + 1], bq1[2 * kp + 1]);

@@ -15,8 +15,12 @@ constexpr int DEC_TILE = 64;    // tokens per pipeline stage (4 warps x 16)
 constexpr int DEC_STAGES = 3;   // TMA ring depth per CTA
 constexpr int DEC_STAGE_BYTES = 2 * DEC_TILE * 256 * 2;  // K + V stage, 64 KB
 constexpr int DEC_XCH_BYTES = 2 * 4 * 8 * 4 * 2 + 2 * 4 * 32 * 8;  // per query row: max, sums, P fragments
+// Per query row: the raw q of the kv head's 6 heads (f32 or bf16, 6 KB max),
+// later overwritten by the normalised bf16 rows [8 heads][256] (4 KB).
+constexpr int DEC_QROW_BYTES = 6 * 1024;
 constexpr int DEC_QS_OFF = DEC_STAGES * DEC_STAGE_BYTES + 3 * DEC_XCH_BYTES + 256;  // after the mbarriers
-constexpr int DEC_SMEM_BYTES = DEC_QS_OFF + 3 * 8 * 256 * 2 + 1024;
+constexpr int DEC_WN_OFF = DEC_QS_OFF + 3 * DEC_QROW_BYTES;                           // q_norm gains, 512 B
+constexpr int DEC_SMEM_BYTES = DEC_WN_OFF + 512 + 1024;
 constexpr int CMB_DIMS_PER_CTA = 8;
 constexpr int CMB_PHASES = 32;
 constexpr int CMB_THREADS = 32 * CMB_PHASES;

@@ -67,6 +67,7 @@ extern "C" int lisa_attn_decode_noalloc(void* k_cache, void* v_cache, uint32_t c
   if (rows != 1 && rows != 3) return LISA_EINVAL;
   if (in_dtype != LISA_DTYPE_F32 && in_dtype != LISA_DTYPE_BF16) return LISA_EINVAL;
   if (capacity == 0 || ((uintptr_t)k_cache & 15) || ((uintptr_t)v_cache & 15)) return LISA_EINVAL;
+  if (((uintptr_t)q_gate & 15) || ((uintptr_t)q_norm_w & 15)) return LISA_EINVAL;
   if ((uint64_t)base + rows > capacity) return LISA_ENOSPC;
   if ((uint64_t)base + rows > NOALLOC_MAX_POS) return LISA_E2BIG;  // beyond the fixed scratch
 

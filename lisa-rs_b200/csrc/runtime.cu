@@ -129,6 +129,8 @@ int run_decode(uint16_t* kc, uint16_t* vc, uint32_t window_rows, uint32_t kv_lo,
   p.win_o = win_o;
   p.win_ml = win_ml;
   if (p.nchunks > chunk_cap) return LISA_EINVAL;
+  // the kernel bulk-copies q rows and the q gains: 16-byte alignment required
+  if (((uintptr_t)q_gate & 15) || ((uintptr_t)qn & 15)) return LISA_EINVAL;
   CUtensorMap tk, tv;
   int s = lisa_encode_kv_map(&tk, kc, p.extent, window_rows, DEC_TILE, KVH);
   if (s == LISA_OK) s = lisa_encode_kv_map(&tv, vc, p.extent, window_rows, DEC_TILE, KVH);
