@@ -8,15 +8,20 @@
 //   gate_out_bf16              attention.metal:520-531  -> prefill_attn_kernel epilogue
 // The reference scans every key serially per (row, head) on scalar lanes; here
 // a CTA owns 128 query rows of one head and runs a flash-attention loop over
-// 64-key tiles of the causal prefix:
-//   warp 0      TMA producer: Q tile once, K/V tiles through a 2-stage ring
-//   warp 1      allocates 512 TMEM columns, issues tcgen05.mma (one thread):
-//               S_j = Q.K_j^T (M128 N64 K256) into a double-buffered TMEM S,
-//               O  += P_j.V_j (M128 N256 K64, V read MN-major)
-//   warps 4..7  softmax: thread = query row = TMEM lane; reads S with
-//               tcgen05.ld, masks causally, keeps an online max that is only
-//               moved (and O rescaled in TMEM) when it grows by more than 2^8,
-//               writes bf16 P to shared memory; epilogue O/l * sigmoid(gate).
+// 64-key tiles of the causal prefix, with every MMA operand that is reused
+// kept in tensor memory (TMEM, 512 columns):
+//   columns [0,256) O accumulator, [256,384) two S tiles, [384,512) Q (bf16)
+//   warp 0       TMA producer: K/V tiles through a 3-stage ring
+//   warp 1       allocates TMEM, issues tcgen05.mma (one thread):
+//                S_j = Q.K_j^T  (A = Q from TMEM, B = K from smem; M128 N64 K256)
+//                O  += P_j.V_j  (A = P from TMEM, B = V from smem read MN-major;
+//                                M128 N256 K64)
+//   warps 4..11  softmax: thread = query row = TMEM lane; warps 4+w and 8+w
+//                share lanes 32w.. and split the columns. They load Q into
+//                TMEM, read S with tcgen05.ld, mask causally, keep an online
+//                max that is only moved (and O rescaled in TMEM) when it grows
+//                by more than 2^8, and write bf16 P over the S tile it came
+//                from; epilogue O/l * sigmoid(gate).
 // Key tiles past the last query row are skipped (causal tile skipping).
 #include <algorithm>
 
@@ -30,46 +35,45 @@ namespace {
 
 constexpr int PF_BM = 128;  // query rows per CTA
 constexpr int PF_BN = 64;   // keys per tile
-constexpr int PF_Q_BYTES = PF_BM * HD * 2;    // 64 KB
-constexpr int PF_KV_BYTES = PF_BN * HD * 2;   // 32 KB
-constexpr int PF_P_BYTES = PF_BM * PF_BN * 2; // 16 KB
-constexpr int PF_OFF_K = PF_Q_BYTES;
-constexpr int PF_OFF_V = PF_OFF_K + 2 * PF_KV_BYTES;
-constexpr int PF_OFF_P = PF_OFF_V + 2 * PF_KV_BYTES;  // two P buffers
-constexpr int PF_OFF_BAR = PF_OFF_P + 2 * PF_P_BYTES;
-constexpr int PF_SMEM_BYTES = PF_OFF_BAR + 256 + 1024;
+constexpr int PF_KV_STAGES = 3;
+constexpr int PF_KV_BYTES = PF_BN * HD * 2;  // 32 KB per K or V tile
+constexpr int PF_OFF_K = 0;
+constexpr int PF_OFF_V = PF_KV_STAGES * PF_KV_BYTES;
+constexpr int PF_OFF_BAR = 2 * PF_KV_STAGES * PF_KV_BYTES;
+constexpr int PF_SMEM_BYTES = PF_OFF_BAR + 2048 + 1024;  // barriers, TMEM slot, row sums
 constexpr int PF_THREADS = 384;  // warp 0 TMA, warp 1 MMA, warps 4..11 softmax
 constexpr uint32_t PF_TMEM_COLS = 512;
 constexpr uint32_t PF_TMEM_O = 0;    // O accumulator: columns [0, 256)
-constexpr uint32_t PF_TMEM_S = 256;  // S buffers: columns [256, 320), [320, 384)
+constexpr uint32_t PF_TMEM_S = 256;  // S / P tiles: columns [256, 320), [320, 384)
+constexpr uint32_t PF_TMEM_Q = 384;  // Q (bf16 pairs): columns [384, 512)
 constexpr float PF_RESCALE_LOG2 = 8.0f;
 
-// Barrier slots inside the barrier block.
-// [2] = one per ring slot / buffer.
+// mbarrier slots ([3]/[2] = one per ring slot / S buffer)
 enum {
-  B_Q = 0,
-  B_KFULL = 1,   // K tile landed
-  B_VFULL = 3,   // V tile landed
-  B_KEMPTY = 5,  // S MMA that read the K slot finished
-  B_VEMPTY = 7,  // PV MMA that read the V slot finished
-  B_SFULL = 9,   // S tile in TMEM
-  B_PFULL = 11,  // P tile in shared memory (128 softmax threads)
-  B_PVDONE = 13, // PV MMA that read the P buffer finished (O updated)
-  B_COUNT = 15
+  B_QT = 0,       // Q stored into TMEM (256 softmax threads)
+  B_KFULL = 1,    // K tile landed
+  B_VFULL = 4,    // V tile landed
+  B_KEMPTY = 7,   // S MMA that read the K slot finished
+  B_VEMPTY = 10,  // PV MMA that read the V slot finished
+  B_SFULL = 13,   // S tile in TMEM
+  B_PFULL = 15,   // P tile in TMEM (256 softmax threads)
+  B_PVDONE = 17,  // PV MMA that read the P tile finished (O updated)
+  B_COUNT = 19
 };
 
 }  // namespace
 
-// One warp per (row, head) item; items 0..27 per row are the 24 query heads
-// then the 4 KV heads. Lane l holds dims 8l..8l+7; the RoPE partner of dims
+// One CTA per prompt row, one warp per item: items 0..23 are the query heads,
+// 24..27 the KV heads. The row's 32 RoPE (cos, sin) pairs are computed once
+// into shared memory. Lane l holds dims 8l..8l+7; the RoPE partner of dims
 // 0..31 (lanes 0..3) is dims 32..63 (lanes 4..7).
-__global__ void __launch_bounds__(256) prefill_prologue_kernel(const PrefillParams p) {
-  const int item = blockIdx.x * 8 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (item >= p.rows * (QH + KVH)) return;
-  const int r = item / (QH + KVH), hh = item % (QH + KVH);
-  const bool is_q = hh < QH;
+__global__ void __launch_bounds__(32 * (QH + KVH)) prefill_prologue_kernel(const PrefillParams p) {
+  __shared__ float s_cos[ROT_PAIRS], s_sin[ROT_PAIRS];
+  const int r = blockIdx.x;
+  const int hh = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t pos = p.base + r;
+  if (threadIdx.x < ROT_PAIRS) rope_cs(pos, p.inv_freq[threadIdx.x], s_cos[threadIdx.x], s_sin[threadIdx.x]);
+  const bool is_q = hh < QH;
   const size_t in = is_q ? (size_t)r * QROW + (size_t)hh * 512 + lane * 8
                          : (size_t)r * KROW + (size_t)(hh - QH) * HD + lane * 8;
   const void* src = is_q ? p.q_gate : p.k_in;
@@ -80,9 +84,15 @@ __global__ void __launch_bounds__(256) prefill_prologue_kernel(const PrefillPara
     x[i] = load_in_bf16(src, in + i, p.in_bf16);
     ss += x[i] * x[i];
   }
+  float v[8];
+  if (!is_q) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = load_in_bf16(p.v_in, in + i, p.in_bf16);
+  }
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
   const float inv = 1.0f / sqrtf(ss / 256.0f + p.eps);
+  __syncthreads();  // RoPE table ready
   float o[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
@@ -90,9 +100,8 @@ __global__ void __launch_bounds__(256) prefill_prologue_kernel(const PrefillPara
     const float partner = __shfl_xor_sync(0xffffffffu, n, 4);
     o[i] = n;
     if (lane < 8) {
-      float c, s;
-      rope_cs(pos, p.inv_freq[(lane & 3) * 8 + i], c, s);
-      o[i] = lane < 4 ? n * c - partner * s : n * c + partner * s;
+      const int j = (lane & 3) * 8 + i;
+      o[i] = lane < 4 ? n * s_cos[j] - partner * s_sin[j] : n * s_cos[j] + partner * s_sin[j];
     }
   }
   const uint4 packed = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
@@ -102,9 +111,6 @@ __global__ void __launch_bounds__(256) prefill_prologue_kernel(const PrefillPara
   } else {
     const size_t out = ((size_t)(hh - QH) * p.capacity + pos) * HD + lane * 8;
     *reinterpret_cast<uint4*>(p.k_cache + out) = packed;
-    float v[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = load_in_bf16(p.v_in, in + i, p.in_bf16);
     *reinterpret_cast<uint4*>(p.v_cache + out) =
         make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
   }
@@ -128,10 +134,10 @@ __device__ __forceinline__ void load8_bf16(const void* src, size_t idx, int is_b
   }
 }
 
-// Grid: n_qtiles * 24 CTAs, heaviest (last) query tiles first. 256 threads.
+// Grid: n_qtiles * 24 CTAs, heaviest (last) query tiles first.
 __global__ void __launch_bounds__(PF_THREADS, 1)
-    prefill_attn_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                        const __grid_constant__ CUtensorMap tv, const PrefillParams p) {
+    prefill_attn_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+                        const PrefillParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + PF_OFF_BAR);
@@ -147,10 +153,10 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
   const int n_tiles = (int)((kv_end + PF_BN - 1) / PF_BN);
 
   if (threadIdx.x == 0) {
-    tma_prefetch_desc(&tq);
     tma_prefetch_desc(&tk);
     tma_prefetch_desc(&tv);
-    for (int b = 0; b < B_COUNT; ++b) mbar_init(&bars[b], (b == B_PFULL || b == B_PFULL + 1) ? 256 : 1);
+    for (int b = 0; b < B_COUNT; ++b)
+      mbar_init(&bars[b], (b == B_QT || b == B_PFULL || b == B_PFULL + 1) ? 256 : 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -161,16 +167,31 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+#ifdef LISA_PREFILL_TRACE
+  unsigned long long tr[8] = {};
+  long long tl = clock64();
+#define PT(k)                        \
+  {                                  \
+    const long long tn = clock64();  \
+    tr[k] += tn - tl;                \
+    tl = tn;                         \
+  }
+#define PT_FLUSH(role)                                                             \
+  if (lane == 0)                                                                   \
+    for (int k = 0; k < 8; ++k) atomicAdd(&p.trace[(role) * 8 + k], tr[k]);
+#else
+#define PT(k)
+#define PT_FLUSH(role)
+#endif
 
   if (warp == 0) {
-    // ---------------- TMA producer, in the order the MMAs need the tiles:
-    // Q, K0, K1, V0, K2, V1, ... ----------------
+    // ---------------- TMA producer: K0, K1, V0, K2, V1, ... (need order) ----------------
     if (lane == 0) {
-      mbar_arrive_expect_tx(&bars[B_Q], PF_Q_BYTES);
-      for (int st = 0; st < 4; ++st) tma_load_3d(smem + st * (PF_BM * 128), &tq, &bars[B_Q], st * 64, r0, h);
       auto load = [&](const CUtensorMap* map, int off, int full, int empty, int j) -> bool {
-        const int s = j & 1;
-        if (j >= 2 && !mbar_wait(&bars[empty + s], ((j >> 1) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) return false;
+        const int s = j % PF_KV_STAGES;
+        if (j >= PF_KV_STAGES &&
+            !mbar_wait(&bars[empty + s], ((j / PF_KV_STAGES) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY))
+          return false;
         uint8_t* dst = smem + off + s * PF_KV_BYTES;
         mbar_arrive_expect_tx(&bars[full + s], PF_KV_BYTES);
         for (int st = 0; st < 4; ++st) tma_load_3d(dst + st * 8192, map, &bars[full + s], st * 64, j * PF_BN, kvh);
@@ -190,42 +211,50 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     if (lane == 0) {
       constexpr uint32_t IDESC_S = umma_idesc_bf16(PF_BM, PF_BN, false);
       constexpr uint32_t IDESC_O = umma_idesc_bf16(PF_BM, HD, true);
-      const uint32_t sQ = smem_u32(smem);
-      bool ok = mbar_wait(&bars[B_Q], 0, p.err, ERR_TIMEOUT_FULL);
+      bool ok = mbar_wait(&bars[B_QT], 0, p.err, ERR_TIMEOUT_FULL);
       auto issue_s = [&](int j) -> bool {
-        const int s = j & 1;
-        if (!mbar_wait(&bars[B_KFULL + s], (j >> 1) & 1, p.err, ERR_TIMEOUT_FULL)) return false;
+        const int s = j % PF_KV_STAGES, b = j & 1;
+        PT(7);
+        if (!mbar_wait(&bars[B_KFULL + s], (j / PF_KV_STAGES) & 1, p.err, ERR_TIMEOUT_FULL)) return false;
+        PT(0);
         tc_fence_after();
         const uint32_t sK = smem_u32(smem + PF_OFF_K + s * PF_KV_BYTES);
-        const uint32_t d = tmem + PF_TMEM_S + s * PF_BN;
+        const uint32_t d = tmem + PF_TMEM_S + b * PF_BN;
 #pragma unroll
         for (int kk = 0; kk < 16; ++kk) {
-          const uint64_t a = umma_desc_sw128(sQ + (kk >> 2) * (PF_BM * 128) + (kk & 3) * 32, 16, 1024);
-          const uint64_t b = umma_desc_sw128(sK + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024);
-          umma_bf16(d, a, b, IDESC_S, kk > 0);
+          const uint64_t bd = umma_desc_sw128(sK + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024);
+          umma_bf16_ts(d, tmem + PF_TMEM_Q + kk * 8, bd, IDESC_S, kk > 0);
         }
-        umma_commit(&bars[B_SFULL + s]);
+        umma_commit(&bars[B_SFULL + b]);
         umma_commit(&bars[B_KEMPTY + s]);
+        PT(1);
         return true;
       };
-      if (ok) ok = issue_s(0);
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        const int s = j & 1;
-        if (j + 1 < n_tiles && !issue_s(j + 1)) break;
-        if (!mbar_wait(&bars[B_PFULL + s], (j >> 1) & 1, p.err, ERR_TIMEOUT_MMA)) break;
-        if (!mbar_wait(&bars[B_VFULL + s], (j >> 1) & 1, p.err, ERR_TIMEOUT_FULL)) break;
+      if (ok) {
         tc_fence_after();
-        const uint32_t sP = smem_u32(smem + PF_OFF_P + s * PF_P_BYTES);
+        ok = issue_s(0);
+      }
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        const int s = j % PF_KV_STAGES, b = j & 1;
+        if (j + 1 < n_tiles && !issue_s(j + 1)) break;
+        PT(7);
+        if (!mbar_wait(&bars[B_PFULL + b], (j >> 1) & 1, p.err, ERR_TIMEOUT_MMA)) break;
+        PT(2);
+        if (!mbar_wait(&bars[B_VFULL + s], (j / PF_KV_STAGES) & 1, p.err, ERR_TIMEOUT_FULL)) break;
+        PT(3);
+        tc_fence_after();
         const uint32_t sV = smem_u32(smem + PF_OFF_V + s * PF_KV_BYTES);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t a = umma_desc_sw128(sP + kk * 32, 16, 1024);
-          const uint64_t b = umma_desc_sw128(sV + kk * 2048, 8192, 1024);
-          umma_bf16(tmem + PF_TMEM_O, a, b, IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+          const uint64_t bd = umma_desc_sw128(sV + kk * 2048, 8192, 1024);
+          umma_bf16_ts(tmem + PF_TMEM_O, tmem + PF_TMEM_S + b * PF_BN + kk * 8, bd, IDESC_O,
+                       (j > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&bars[B_PVDONE + s]);
+        umma_commit(&bars[B_PVDONE + b]);
         umma_commit(&bars[B_VEMPTY + s]);
+        PT(4);
       }
+      PT_FLUSH(0);
     }
     __syncwarp();
     named_bar_sync(1, 288);
@@ -245,14 +274,32 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
   const int row = wi * 32 + lane;  // row within the tile == TMEM lane
   const uint32_t lane_addr = tmem + ((uint32_t)(wi * 32) << 16);
   const uint32_t pos_row = p.base + (uint32_t)(r0 + row);
-  float m2 = -INFINITY, l = 0.f;  // running max (log2 domain), this half's sum
   bool ok = true;
+  {
+    // Q row (bf16) into TMEM columns [384 + 64*half, +64)
+    const uint4* src = reinterpret_cast<const uint4*>(p.q_ws + ((size_t)h * PF_MAX_ROWS + r0 + row) * HD + half * 128);
+    uint32_t qa[32], qb[32];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint4 a = src[i], b = src[8 + i];
+      qa[4 * i] = a.x; qa[4 * i + 1] = a.y; qa[4 * i + 2] = a.z; qa[4 * i + 3] = a.w;
+      qb[4 * i] = b.x; qb[4 * i + 1] = b.y; qb[4 * i + 2] = b.z; qb[4 * i + 3] = b.w;
+    }
+    tmem_st32(lane_addr + PF_TMEM_Q + half * 64, qa);
+    tmem_st32(lane_addr + PF_TMEM_Q + half * 64 + 32, qb);
+    tmem_wait_st();
+    tc_fence_before();
+    mbar_arrive(&bars[B_QT]);
+  }
+  float m2 = -INFINITY, l = 0.f;  // running max (log2 domain), this half's sum
   for (int j = 0; j < n_tiles; ++j) {
     const int b = j & 1;
+    PT(7);
     if (!mbar_wait(&bars[B_SFULL + b], (j >> 1) & 1, p.err, ERR_TIMEOUT_MMA)) {
       ok = false;
       break;
     }
+    PT(0);
     tc_fence_after();
     uint32_t sa[32], sb[32];
     tmem_ld32(lane_addr + PF_TMEM_S + b * PF_BN, sa);
@@ -286,9 +333,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     for (int c = 0; c < 16; ++c) {
       const float x0 = half ? s2[32 + 2 * c] : s2[2 * c];
       const float x1 = half ? s2[33 + 2 * c] : s2[2 * c + 1];
-      const float e0 = fast_exp2(x0 - m2);
-      const float e1 = fast_exp2(x1 - m2);
-      pk[c] = pack_bf16x2(e0, e1);
+      pk[c] = pack_bf16x2(fast_exp2(x0 - m2), fast_exp2(x1 - m2));
       ps[c] = bf16_bits_to_f32(pk[c] & 0xffffu) + bf16_bits_to_f32(pk[c] >> 16);
     }
 #pragma unroll
@@ -296,6 +341,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 #pragma unroll
       for (int c = 0; c < w; ++c) ps[c] += ps[c + w];
     l = l * alpha + ps[0];
+    PT(1);
     if (j > 0 && __any_sync(0xffffffffu, need)) {
       // O must hold exactly tiles < j before it is rescaled
       if (!mbar_wait(&bars[B_PVDONE + (b ^ 1)], ((j - 1) >> 1) & 1, p.err, ERR_TIMEOUT_MMA)) {
@@ -315,33 +361,40 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
       }
       tmem_wait_st();
     }
-    if (j >= 2 && !mbar_wait(&bars[B_PVDONE + b], ((j - 2) >> 1) & 1, p.err, ERR_TIMEOUT_MMA)) {
-      ok = false;  // P buffer b is free once PV_{j-2} finished
-      break;
-    }
-    uint8_t* sP = smem + PF_OFF_P + b * PF_P_BYTES;
-#pragma unroll
-    for (int c = 0; c < 4; ++c)
-      *reinterpret_cast<uint4*>(sP + swz128((uint32_t)row, (uint32_t)(half * 4 + c))) =
-          make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-    fence_proxy_async_smem();
+    PT(2);
+    // both halves have read this S tile before P overwrites its first 32 columns
+    named_bar_sync(2 + wi, 64);
+    PT(3);
+    tmem_st16(lane_addr + PF_TMEM_S + b * PF_BN + half * 16, pk);
+    tmem_wait_st();
     tc_fence_before();
     mbar_arrive(&bars[B_PFULL + b]);
+    PT(4);
+  }
+  // gate values of this row and half, prefetched while the last P.V runs
+  const int r = r0 + row;
+  uint32_t gpk[64];
+  if (ok && r < p.rows) {
+    const size_t gbase = (size_t)r * QROW + (size_t)h * 512 + 256 + half * 128;
+#pragma unroll
+    for (int g8 = 0; g8 < 16; ++g8) {
+      float gv[8];
+      load8_bf16(p.q_gate, gbase + g8 * 8, p.in_bf16, gv);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) gpk[g8 * 4 + i] = pack_bf16x2(gv[2 * i], gv[2 * i + 1]);
+    }
   }
   const int last = n_tiles - 1;
   ok = ok && mbar_wait(&bars[B_PVDONE + (last & 1)], (last >> 1) & 1, p.err, ERR_TIMEOUT_MMA);
-  // Sum the two halves' denominators (half 0 + half 1) through the now idle
-  // P buffers.
-  float* lx = reinterpret_cast<float*>(smem + PF_OFF_P);
+  // Sum the two halves' denominators (half 0 + half 1).
+  float* lx = reinterpret_cast<float*>(smem + PF_OFF_BAR + 256);
   lx[half * PF_BM + row] = l;
   named_bar_sync(2 + wi, 64);
   const float l_row = lx[row] + lx[PF_BM + row];
   if (ok) {
     tc_fence_after();
-    const int r = r0 + row;
     const float inv_l = 1.0f / l_row;
-    const size_t gbase = (size_t)r * QROW + (size_t)h * 512 + 256;
-#pragma unroll 1
+#pragma unroll
     for (int c = 0; c < HD / 64; ++c) {
       const int col = half * (HD / 2) + c * 32;
       uint32_t ov[32];
@@ -350,19 +403,16 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
       if (r < p.rows) {
         uint32_t outw[16];
 #pragma unroll
-        for (int g8 = 0; g8 < 4; ++g8) {
-          float gv[8];
-          load8_bf16(p.q_gate, gbase + col + g8 * 8, p.in_bf16, gv);
+        for (int i = 0; i < 16; ++i) {
+          const uint32_t gg = gpk[c * 16 + i];
+          float y[2];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            float y[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const float sg = 1.0f / (1.0f + exp2f(-LOG2E * gv[2 * i + e]));
-              y[e] = __uint_as_float(ov[g8 * 8 + 2 * i + e]) * inv_l * sg;
-            }
-            outw[g8 * 4 + i] = pack_bf16x2(y[0], y[1]);
+          for (int e = 0; e < 2; ++e) {
+            const float gv = bf16_bits_to_f32(e ? gg >> 16 : gg & 0xffffu);
+            const float sg = 1.0f / (1.0f + exp2f(-LOG2E * gv));
+            y[e] = __uint_as_float(ov[2 * i + e]) * inv_l * sg;
           }
+          outw[i] = pack_bf16x2(y[0], y[1]);
         }
         uint4* dst = reinterpret_cast<uint4*>(p.gated_out + (size_t)r * OROW + h * HD + col);
 #pragma unroll
@@ -370,6 +420,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
       }
     }
   }
+  PT(5);
+  if (warp == 4) { PT_FLUSH(1); }
   tc_fence_before();
   named_bar_sync(1, 288);
 }
@@ -380,8 +432,7 @@ cudaError_t launch_prefill(const PrefillParams& p_in, int num_sms, cudaStream_t 
   (void)num_sms;
   PrefillParams p = p_in;
   host_inv_freq(p.inv_freq);
-  const int items = p.rows * (QH + KVH);
-  prefill_prologue_kernel<<<(items + 7) / 8, 256, 0, stream>>>(p);
+  prefill_prologue_kernel<<<p.rows, 32 * (QH + KVH), 0, stream>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   static bool configured = false;
@@ -390,14 +441,13 @@ cudaError_t launch_prefill(const PrefillParams& p_in, int num_sms, cudaStream_t 
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tk, tv;
   const uint32_t kv_rows = p.base + (uint32_t)p.rows;
-  if (lisa_encode_kv_map(&tq, p.q_ws, PF_MAX_ROWS, PF_MAX_ROWS, PF_BM, QH) != 0 ||
-      lisa_encode_kv_map(&tk, p.k_cache, kv_rows, p.capacity, PF_BN, KVH) != 0 ||
+  if (lisa_encode_kv_map(&tk, p.k_cache, kv_rows, p.capacity, PF_BN, KVH) != 0 ||
       lisa_encode_kv_map(&tv, p.v_cache, kv_rows, p.capacity, PF_BN, KVH) != 0)
     return cudaErrorInvalidValue;
   const int n_qt = (p.rows + PF_BM - 1) / PF_BM;
-  prefill_attn_kernel<<<n_qt * QH, PF_THREADS, PF_SMEM_BYTES, stream>>>(tq, tk, tv, p);
+  prefill_attn_kernel<<<n_qt * QH, PF_THREADS, PF_SMEM_BYTES, stream>>>(tk, tv, p);
   return cudaGetLastError();
 }
 

@@ -31,6 +31,9 @@ struct PrefillParams {
   uint16_t* gated_out;  // [rows][6144]
   int* err;
   float inv_freq[32];  // filled by launch_prefill
+#ifdef LISA_PREFILL_TRACE
+  unsigned long long* trace;  // debug builds only
+#endif
 };
 
 // Bytes of device workspace launch_prefill needs.
