@@ -78,6 +78,13 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// 1/x on the SFU (rcp.approx, about 1 ulp).
+__device__ __forceinline__ float fast_rcp(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ uint64_t global_timer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

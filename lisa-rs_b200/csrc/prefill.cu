@@ -63,61 +63,8 @@ enum {
 
 }  // namespace
 
-// One CTA per prompt row, one warp per item: items 0..23 are the query heads,
-// 24..27 the KV heads. The row's 32 RoPE (cos, sin) pairs are computed once
-// into shared memory. Lane l holds dims 8l..8l+7; the RoPE partner of dims
-// 0..31 (lanes 0..3) is dims 32..63 (lanes 4..7).
-__global__ void __launch_bounds__(32 * (QH + KVH)) prefill_prologue_kernel(const PrefillParams p) {
-  __shared__ float s_cos[ROT_PAIRS], s_sin[ROT_PAIRS];
-  const int r = blockIdx.x;
-  const int hh = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t pos = p.base + r;
-  if (threadIdx.x < ROT_PAIRS) rope_cs(pos, p.inv_freq[threadIdx.x], s_cos[threadIdx.x], s_sin[threadIdx.x]);
-  const bool is_q = hh < QH;
-  const size_t in = is_q ? (size_t)r * QROW + (size_t)hh * 512 + lane * 8
-                         : (size_t)r * KROW + (size_t)(hh - QH) * HD + lane * 8;
-  const void* src = is_q ? p.q_gate : p.k_in;
-  const uint16_t* w = is_q ? p.q_norm_w : p.k_norm_w;
-  float x[8], ss = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    x[i] = load_in_bf16(src, in + i, p.in_bf16);
-    ss += x[i] * x[i];
-  }
-  float v[8];
-  if (!is_q) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = load_in_bf16(p.v_in, in + i, p.in_bf16);
-  }
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-  const float inv = 1.0f / sqrtf(ss / 256.0f + p.eps);
-  __syncthreads();  // RoPE table ready
-  float o[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float n = x[i] * inv * bf16_bits_to_f32(w[lane * 8 + i]);
-    const float partner = __shfl_xor_sync(0xffffffffu, n, 4);
-    o[i] = n;
-    if (lane < 8) {
-      const int j = (lane & 3) * 8 + i;
-      o[i] = lane < 4 ? n * s_cos[j] - partner * s_sin[j] : n * s_cos[j] + partner * s_sin[j];
-    }
-  }
-  const uint4 packed = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
-                                  pack_bf16x2(o[6], o[7]));
-  if (is_q) {
-    *reinterpret_cast<uint4*>(p.q_ws + ((size_t)hh * PF_MAX_ROWS + r) * HD + lane * 8) = packed;
-  } else {
-    const size_t out = ((size_t)(hh - QH) * p.capacity + pos) * HD + lane * 8;
-    *reinterpret_cast<uint4*>(p.k_cache + out) = packed;
-    *reinterpret_cast<uint4*>(p.v_cache + out) =
-        make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
-  }
-}
-
 // Eight consecutive inputs rounded to bf16, vectorised (idx multiple of 8).
-__device__ __forceinline__ void load8_bf16(const void* src, size_t idx, int is_bf16, float (&out)[8]) {
+__device__ __forceinline__ void load8_in(const void* src, size_t idx, int is_bf16, float (&out)[8]) {
   if (is_bf16) {
     const uint4 w = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(src) + idx);
     const uint32_t u[4] = {w.x, w.y, w.z, w.w};
@@ -131,6 +78,71 @@ __device__ __forceinline__ void load8_bf16(const void* src, size_t idx, int is_b
     const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(src) + idx + 4);
     out[0] = round_bf16(a.x); out[1] = round_bf16(a.y); out[2] = round_bf16(a.z); out[3] = round_bf16(a.w);
     out[4] = round_bf16(b.x); out[5] = round_bf16(b.y); out[6] = round_bf16(b.z); out[7] = round_bf16(b.w);
+  }
+}
+
+// One 256-thread CTA per prompt row; warp w handles items w, w+8, w+16, w+24
+// (items 0..23 are the query heads, 24..27 the KV heads). The row's 32 RoPE
+// (cos, sin) pairs are computed once into shared memory while the loads are in
+// flight. Lane l holds dims 8l..8l+7; the RoPE partner of dims 0..31
+// (lanes 0..3) is dims 32..63 (lanes 4..7).
+__global__ void __launch_bounds__(256) prefill_prologue_kernel(const PrefillParams p) {
+  __shared__ float s_cos[ROT_PAIRS], s_sin[ROT_PAIRS];
+  pdl_wait_primary();       // the previous chunk may still read q_ws
+  pdl_launch_dependents();  // let the attention kernel set up meanwhile
+  const int r = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t pos = p.base + r;
+  constexpr int NI = 4;  // items per warp
+  float x[NI][8], v[NI][8];  // v: the V row of KV items
+#pragma unroll
+  for (int t = 0; t < NI; ++t) {
+    const int hh = warp + 8 * t;
+    if (hh >= QH + KVH) continue;
+    const bool is_q = hh < QH;
+    const size_t in = is_q ? (size_t)r * QROW + (size_t)hh * 512 + lane * 8
+                           : (size_t)r * KROW + (size_t)(hh - QH) * HD + lane * 8;
+    load8_in(is_q ? p.q_gate : p.k_in, in, p.in_bf16, x[t]);
+    if (!is_q) load8_in(p.v_in, in, p.in_bf16, v[t]);
+  }
+  if (threadIdx.x < ROT_PAIRS) rope_cs(pos, p.inv_freq[threadIdx.x], s_cos[threadIdx.x], s_sin[threadIdx.x]);
+  __syncthreads();  // RoPE table ready
+#pragma unroll
+  for (int t = 0; t < NI; ++t) {
+    const int hh = warp + 8 * t;
+    if (hh >= QH + KVH) continue;  // uniform per warp
+    const bool is_q = hh < QH;
+    const uint16_t* w = is_q ? p.q_norm_w : p.k_norm_w;
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += x[t][i] * x[t][i];
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    const float inv = 1.0f / sqrtf(ss / 256.0f + p.eps);
+    float o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float n = x[t][i] * inv * bf16_bits_to_f32(w[lane * 8 + i]);
+      const float partner = __shfl_xor_sync(0xffffffffu, n, 4);
+      o[i] = n;
+      if (lane < 8) {
+        const int j = (lane & 3) * 8 + i;
+        o[i] = lane < 4 ? n * s_cos[j] - partner * s_sin[j] : n * s_cos[j] + partner * s_sin[j];
+      }
+    }
+    const uint4 packed = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
+                                    pack_bf16x2(o[6], o[7]));
+    if (is_q) {
+      // chunk-major [head][chunk = lane][row]: a warp reading 32 rows of one
+      // chunk touches 512 contiguous bytes
+      *reinterpret_cast<uint4*>(p.q_ws + (((size_t)hh * 32 + lane) * PF_MAX_ROWS + r) * 8) = packed;
+    } else {
+      const size_t out = ((size_t)(hh - QH) * p.capacity + pos) * HD + lane * 8;
+      *reinterpret_cast<uint4*>(p.k_cache + out) = packed;
+      *reinterpret_cast<uint4*>(p.v_cache + out) =
+          make_uint4(pack_bf16x2(v[t][0], v[t][1]), pack_bf16x2(v[t][2], v[t][3]), pack_bf16x2(v[t][4], v[t][5]),
+                     pack_bf16x2(v[t][6], v[t][7]));
+    }
   }
 }
 
@@ -152,6 +164,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
   const uint32_t kv_end = p.base + (uint32_t)r_end;  // keys [0, kv_end)
   const int n_tiles = (int)((kv_end + PF_BN - 1) / PF_BN);
 
+#ifdef LISA_PREFILL_TRACE
+  if (threadIdx.x == 0) p.trace[64 + blockIdx.x * 8 + 0] = global_timer_ns();
+#endif
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tk);
     tma_prefetch_desc(&tv);
@@ -167,7 +182,12 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Setup above overlaps the prologue kernel; its q_ws / KV writes are read
+  // only after it has completed.
+  pdl_wait_primary();
+  pdl_launch_dependents();
 #ifdef LISA_PREFILL_TRACE
+  if (threadIdx.x == 0) p.trace[64 + blockIdx.x * 8 + 1] = global_timer_ns();
   unsigned long long tr[8] = {};
   long long tl = clock64();
 #define PT(k)                        \
@@ -277,11 +297,11 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
   bool ok = true;
   {
     // Q row (bf16) into TMEM columns [384 + 64*half, +64)
-    const uint4* src = reinterpret_cast<const uint4*>(p.q_ws + ((size_t)h * PF_MAX_ROWS + r0 + row) * HD + half * 128);
+    const uint4* src = reinterpret_cast<const uint4*>(p.q_ws) + ((size_t)h * 32 + half * 16) * PF_MAX_ROWS + r0 + row;
     uint32_t qa[32], qb[32];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const uint4 a = src[i], b = src[8 + i];
+      const uint4 a = src[(size_t)i * PF_MAX_ROWS], b = src[(size_t)(8 + i) * PF_MAX_ROWS];
       qa[4 * i] = a.x; qa[4 * i + 1] = a.y; qa[4 * i + 2] = a.z; qa[4 * i + 3] = a.w;
       qb[4 * i] = b.x; qb[4 * i + 1] = b.y; qb[4 * i + 2] = b.z; qb[4 * i + 3] = b.w;
     }
@@ -290,6 +310,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     tmem_wait_st();
     tc_fence_before();
     mbar_arrive(&bars[B_QT]);
+#ifdef LISA_PREFILL_TRACE
+    if (threadIdx.x == 128) p.trace[64 + blockIdx.x * 8 + 2] = global_timer_ns();
+#endif
   }
   float m2 = -INFINITY, l = 0.f;  // running max (log2 domain), this half's sum
   for (int j = 0; j < n_tiles; ++j) {
@@ -371,6 +394,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     mbar_arrive(&bars[B_PFULL + b]);
     PT(4);
   }
+#ifdef LISA_PREFILL_TRACE
+  if (threadIdx.x == 128) p.trace[64 + blockIdx.x * 8 + 3] = global_timer_ns();
+#endif
   // gate values of this row and half, prefetched while the last P.V runs
   const int r = r0 + row;
   uint32_t gpk[64];
@@ -379,7 +405,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 #pragma unroll
     for (int g8 = 0; g8 < 16; ++g8) {
       float gv[8];
-      load8_bf16(p.q_gate, gbase + g8 * 8, p.in_bf16, gv);
+      load8_in(p.q_gate, gbase + g8 * 8, p.in_bf16, gv);
 #pragma unroll
       for (int i = 0; i < 4; ++i) gpk[g8 * 4 + i] = pack_bf16x2(gv[2 * i], gv[2 * i + 1]);
     }
@@ -409,7 +435,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
             const float gv = bf16_bits_to_f32(e ? gg >> 16 : gg & 0xffffu);
-            const float sg = 1.0f / (1.0f + exp2f(-LOG2E * gv));
+            const float sg = fast_rcp(1.0f + fast_exp2(-LOG2E * gv));
             y[e] = __uint_as_float(ov[2 * i + e]) * inv_l * sg;
           }
           outw[i] = pack_bf16x2(y[0], y[1]);
@@ -422,6 +448,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
   }
   PT(5);
   if (warp == 4) { PT_FLUSH(1); }
+#ifdef LISA_PREFILL_TRACE
+  if (threadIdx.x == 128) p.trace[64 + blockIdx.x * 8 + 4] = global_timer_ns();
+#endif
   tc_fence_before();
   named_bar_sync(1, 288);
 }
@@ -432,8 +461,16 @@ cudaError_t launch_prefill(const PrefillParams& p_in, int num_sms, cudaStream_t 
   (void)num_sms;
   PrefillParams p = p_in;
   host_inv_freq(p.inv_freq);
-  prefill_prologue_kernel<<<p.rows, 32 * (QH + KVH), 0, stream>>>(p);
-  cudaError_t e = cudaGetLastError();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.rows);
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, prefill_prologue_kernel, p);
   if (e != cudaSuccess) return e;
   static bool configured = false;
   if (!configured) {
@@ -447,8 +484,10 @@ cudaError_t launch_prefill(const PrefillParams& p_in, int num_sms, cudaStream_t 
       lisa_encode_kv_map(&tv, p.v_cache, kv_rows, p.capacity, PF_BN, KVH) != 0)
     return cudaErrorInvalidValue;
   const int n_qt = (p.rows + PF_BM - 1) / PF_BM;
-  prefill_attn_kernel<<<n_qt * QH, PF_THREADS, PF_SMEM_BYTES, stream>>>(tk, tv, p);
-  return cudaGetLastError();
+  cfg.gridDim = dim3(n_qt * QH);
+  cfg.blockDim = dim3(PF_THREADS);
+  cfg.dynamicSmemBytes = PF_SMEM_BYTES;
+  return cudaLaunchKernelEx(&cfg, prefill_attn_kernel, tk, tv, p);
 }
 
 }  // namespace lisa
