@@ -322,6 +322,119 @@ def cpu_baseline_decode(seconds: float = 8.0, threads: int | None = None):
     return statistics.median(times) * 1e6, O.num_threads(), len(times)
 
 
+def fill_random(t, gen):
+    """Seeded N(0,1) bf16 into a large cache tensor without materialising it
+    twice: a 64 MB random pool copied with shifting offsets."""
+    import torch
+
+    flat = t.view(-1)
+    pool = torch.randn(32 << 20, generator=gen, device=t.device).to(torch.bfloat16)
+    off, k = 0, 0
+    while off < flat.numel():
+        n = min(pool.numel() - (k * 4097) % 4096, flat.numel() - off)
+        start = (k * 4097) % 4096
+        flat[off:off + n].copy_(pool[start:start + n])
+        off += n
+        k += 1
+
+
+def bench_longctx(args, rank, world, local):
+    """one sequence of 262144 positions, M=1 decode of one
+    layer, KV split over the ranks (lisa_split windows) with one all-gather of
+    partials per step. Strong scaling: value = µs per decode step."""
+    import torch
+
+    import lisa_attn
+    import lisa_split
+
+    cap = 262144
+    base = cap - 1
+    stream = torch.cuda.current_stream()
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(0x5EED + 4 + rank)
+    win = lisa_split.plan_windows(cap, world)[rank]
+    dec = lisa_split.SplitKVDecoder(win, max_rows=1)
+    fill_random(dec.k, gen)
+    fill_random(dec.v, gen)
+    w = make_weights(gen, 1)[0]
+    g0 = torch.Generator(device="cuda")
+    g0.manual_seed(0x5EED)  # identical inputs on every rank
+    q = torch.randn((1, QROW), generator=g0, device="cuda")
+    k = torch.randn((1, KROW), generator=g0, device="cuda")
+    v = torch.randn((1, KROW), generator=g0, device="cuda")
+    out = torch.empty((1, OROW), dtype=torch.bfloat16, device="cuda")
+
+    def step():
+        dec.decode(base, q, k, v, w, out, stream)
+
+    with ClockSampler(local) as clk:
+        t_end = time.perf_counter() + 1.0
+        while time.perf_counter() < t_end:
+            for _ in range(10):
+                step()
+            torch.cuda.synchronize()
+        ms = timed(step, args.steps, args.warmup, world, stream)
+    return {"ms": ms, "clocks": clk.summary(), "bytes": 4096 * cap}
+
+
+def bench_batched(args, rank, world, local):
+    """64 sequences, contexts U[1024, 32768] (seeded), 16
+    attention layers each, M=1; sequences sharded over ranks (lisa_split
+    plan_sequences), no collective. value = µs per layer step (all 64
+    sequences through one layer)."""
+    import numpy as np
+    import torch
+
+    import lisa_attn
+    import lisa_split
+
+    rng = np.random.default_rng(0x5EED + 3)
+    ctx = rng.integers(1024, 32769, size=64).tolist()
+    mine = lisa_split.plan_sequences(ctx, world)[rank]
+    stream = torch.cuda.current_stream()
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(0x5EED + 30 + rank)
+    runners = []
+    for i in mine:
+        r = lisa_attn.AttnRunner(LAYERS, ctx[i])
+        for layer in range(LAYERS):
+            kc, vc = r.kv_cache(layer)
+            fill_random(kc, gen)
+            fill_random(vc, gen)
+        runners.append((r, ctx[i] - 1))
+    ws = make_weights(gen, LAYERS)
+    q = torch.randn((1, QROW), generator=gen, device="cuda")
+    k = torch.randn((1, KROW), generator=gen, device="cuda")
+    v = torch.randn((1, KROW), generator=gen, device="cuda")
+    out = torch.empty((1, OROW), dtype=torch.bfloat16, device="cuda")
+
+    def step_eager():
+        for layer in range(LAYERS):
+            for r, base in runners:
+                r.decode_layer(layer, base, 1, q, k, v, ws[layer], out, stream)
+
+    # One step is ~1000 library calls; replaying it as a CUDA graph removes the
+    # Python call overhead from the measurement (the kernels are the same).
+    step_eager()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    cap_stream = torch.cuda.Stream()
+    with torch.cuda.stream(cap_stream):
+        with torch.cuda.graph(graph, stream=cap_stream):
+            for layer in range(LAYERS):
+                for r, base in runners:
+                    r.decode_layer(layer, base, 1, q, k, v, ws[layer], out, cap_stream)
+    torch.cuda.synchronize()
+
+    def step():
+        graph.replay()
+
+    with ClockSampler(local) as clk:
+        ms = timed(step, args.steps, args.warmup, world, stream)
+    total_ctx = sum(ctx)
+    return {"ms": ms, "clocks": clk.summary(), "bytes": 4096 * total_ctx * LAYERS, "ctx_sum": total_ctx}
+
+
 def emit(line: dict) -> None:
     print(json.dumps(line), flush=True)
 
@@ -359,7 +472,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode32k", choices=["decode32k"])
+    ap.add_argument("--workload", default="decode32k", choices=["decode32k", "batched", "longctx"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -374,6 +487,30 @@ def main():
 
     rank, world, local = dist_setup()
     pk = peaks()
+    if args.workload in ("batched", "longctx"):
+        fn = bench_batched if args.workload == "batched" else bench_longctx
+        r = fn(args, rank, world, local)
+        if rank == 0:
+            step_us = r["ms"] * 1000.0 / args.steps
+            value = step_us / LAYERS if args.workload == "batched" else step_us
+            gbs = r["bytes"] / (step_us * 1e-6) / 1e9
+            emit({"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                  "warmup": args.warmup, "ms_per_step": round(step_us / 1000, 4), "higher_is_better": False,
+                  "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                  "config": {"workload": args.workload + (
+                      ": config 3, 64 sequences ctx U[1024,32768] (sum %d), 16 layers, sequences sharded, one CUDA graph per step"
+                      % r["ctx_sum"] if args.workload == "batched" else
+                      ": config 4, ctx 262144 M=1, KV split over ranks, one all-gather of partials"),
+                      "parallelism": f"{world} ranks"},
+                  "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"] * world,
+                               "unit": "GB/s", "frac": round(gbs / (pk["hbm_gbs"] * world), 4), "traffic": None,
+                               "peak_source": pk["source"], "note": "whole job, peak = ranks x measured HBM"},
+                  "clocks": r["clocks"]})
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return
     r = bench_decode32k(args, rank, world, local)
     pf_ms = bench_prefill(args, world)
     cpu = None
