@@ -38,6 +38,10 @@ LAYERS = 16
 CTX = 32768
 PREFILL_TOKENS, PREFILL_CHUNK = 4096, 512
 PREFILL_FLOP = 4 * QH * HD * sum(range(1, PREFILL_TOKENS + 1))  # causal-exact QK^T + PV
+# DRAM bytes of one decode layer call at ctx 32768 (split kernel read 134.30 MB
+# + write 5.93 MB, combine read 8.50 MB), from the ncu capture summarised in
+# profiles/decode_split_kernel_ctx32768.md.
+DECODE_TRAFFIC_32K = 148.73e6
 
 
 def peaks():
@@ -524,7 +528,9 @@ def main():
     value = r["ms"] * 1000.0 / args.steps / layers_total  # aggregate µs per sequence-layer
     e2e = r["ms_e2e"] * 1000.0 / args.steps / layers_total
     layer_bytes = decode_bytes(CTX, 1)
-    achieved = layer_bytes / (r["layer_ms"] * 1e-3) / 1e9
+    # average duration of one layer call (split + combine) over the timed
+    # region: K steps x 16 back-to-back calls, CUDA events on the stream
+    achieved = layer_bytes / (value * 1e-6) / 1e9
     pf_tflops = PREFILL_FLOP / (pf_ms / args.steps * 1e-3) / 1e12
     emit({
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -535,9 +541,10 @@ def main():
                    "sequences": world, "parallelism": f"sequences sharded, dp{world}, no collective",
                    "l2": "inputs larger than L2 (16 x 134 MB KV per step)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None, "peak_source": pk["source"],
+                     "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": DECODE_TRAFFIC_32K, "peak_source": pk["source"],
                      "kernel": "decode_split_kernel<1> + decode_combine_kernel (one layer call)",
-                     "algorithmic_bytes": layer_bytes, "layer_us": round(r["layer_ms"] * 1000, 3)},
+                     "algorithmic_bytes": layer_bytes, "layer_us_timed": round(value, 3),
+                     "layer_us_isolated": round(r["layer_ms"] * 1000, 3)},
         "cpu_baseline": cpu,
         "e2e": {"value": round(e2e, 3), "unit": UNIT, "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
         "gpu_launches": 2 * LAYERS * args.steps,
@@ -546,6 +553,9 @@ def main():
                     "tflops": round(pf_tflops, 2), "flop": PREFILL_FLOP,
                     "frac_burst": round(pf_tflops / pk["bf16_tflops"], 4),
                     "frac_sustained": round(pf_tflops / pk["bf16_tflops_sustained"], 4),
+                    "roofline": {"bound": "tensor", "achieved": round(pf_tflops, 2), "peak": pk["bf16_tflops"],
+                                 "unit": "TFLOP/s", "frac": round(pf_tflops / pk["bf16_tflops"], 4), "traffic": None,
+                                 "kernel": "prefill_prologue_kernel + prefill_attn_kernel, 8 chunk calls"},
                     "gpu_launches_per_step": 2 * (PREFILL_TOKENS // PREFILL_CHUNK)},
     })
     if world > 1:
