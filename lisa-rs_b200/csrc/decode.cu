@@ -42,13 +42,15 @@ __device__ __forceinline__ uint32_t chunk_tiles(uint32_t chunk, uint32_t extent)
 
 // Issues the TMA loads of one 64-token stage: K and V, 4 boxes of 64 dims
 // (128-byte swizzled rows) each.
+// The KV stream is read once: it is loaded with an evict-first L2 policy so
+// it does not push the chunk partials (read back by the combine) out of L2.
 __device__ __forceinline__ void issue_tile(uint8_t* stage, uint64_t* full, const CUtensorMap* tk,
-                                           const CUtensorMap* tv, uint32_t row0, int kvh) {
+                                           const CUtensorMap* tv, uint32_t row0, int kvh, uint64_t pol) {
   mbar_arrive_expect_tx(full, DEC_STAGE_BYTES);
 #pragma unroll
   for (int st = 0; st < 4; ++st) {
-    tma_load_3d(stage + st * (DEC_TILE * 128), tk, full, st * 64, (int)row0, kvh);
-    tma_load_3d(stage + DEC_STAGE_BYTES / 2 + st * (DEC_TILE * 128), tv, full, st * 64, (int)row0, kvh);
+    tma_load_3d_hint(stage + st * (DEC_TILE * 128), tk, full, st * 64, (int)row0, kvh, pol);
+    tma_load_3d_hint(stage + DEC_STAGE_BYTES / 2 + st * (DEC_TILE * 128), tv, full, st * 64, (int)row0, kvh, pol);
   }
 }
 
@@ -155,6 +157,7 @@ __global__ void __launch_bounds__(32 * (4 * ROWS + 1), 1)
       // a chunk's numerics do not depend on which CTA runs it.
       uint32_t i = 0;
       bool done = false;
+      const uint64_t pol = l2_policy_evict_first();
       while (!done) {
         const uint32_t chunk = atomicAdd(&p.sched[kvh], 1u);
         done = chunk >= p.nchunks;
@@ -170,7 +173,8 @@ __global__ void __launch_bounds__(32 * (4 * ROWS + 1), 1)
             mbar_arrive(&full[slot]);  // end marker, no data
             break;
           }
-          issue_tile(smem + slot * DEC_STAGE_BYTES, &full[slot], &tk, &tv, chunk * DEC_CHUNK + t * DEC_TILE, kvh);
+          issue_tile(smem + slot * DEC_STAGE_BYTES, &full[slot], &tk, &tv, chunk * DEC_CHUNK + t * DEC_TILE, kvh,
+                     pol);
         }
       }
     }
