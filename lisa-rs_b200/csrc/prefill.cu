@@ -33,33 +33,35 @@ namespace lisa {
 
 namespace {
 
-constexpr int PF_BM = 128;  // query rows per CTA
-constexpr int PF_BN = 64;   // keys per tile
-constexpr int PF_KV_STAGES = 3;
-constexpr int PF_KV_BYTES = PF_BN * HD * 2;  // 32 KB per K or V tile
-constexpr int PF_OFF_K = 0;
-constexpr int PF_OFF_V = PF_KV_STAGES * PF_KV_BYTES;
-constexpr int PF_OFF_BAR = 2 * PF_KV_STAGES * PF_KV_BYTES;
-constexpr int PF_SMEM_BYTES = PF_OFF_BAR + 2048 + 1024;  // barriers, TMEM slot, row sums
+constexpr int PF_BM = 128;   // query rows per CTA
+constexpr int PF_BN = 128;   // keys per tile
+constexpr int PF_SLOT = 16384;  // ring slot: K sub-tile [128 keys][64 dims] or V sub-tile [32 keys][256 dims]
+constexpr int PF_RING = 9;
+constexpr int PF_Q_BYTES = PF_BM * HD * 2;  // 64 KB
+constexpr int PF_OFF_RING = PF_Q_BYTES;
+constexpr int PF_OFF_BAR = PF_OFF_RING + PF_RING * PF_SLOT;
+constexpr int PF_SMEM_BYTES = PF_OFF_BAR + 4096 + 1024;  // barriers, TMEM slot, max/sum exchange
 constexpr int PF_THREADS = 384;  // warp 0 TMA, warp 1 MMA, warps 4..11 softmax
 constexpr uint32_t PF_TMEM_COLS = 512;
 constexpr uint32_t PF_TMEM_O = 0;    // O accumulator: columns [0, 256)
-constexpr uint32_t PF_TMEM_S = 256;  // S / P tiles: columns [256, 320), [320, 384)
-constexpr uint32_t PF_TMEM_Q = 384;  // Q (bf16 pairs): columns [384, 512)
+constexpr uint32_t PF_TMEM_S = 256;  // S / P tiles: columns [256, 384), [384, 512)
 constexpr float PF_RESCALE_LOG2 = 8.0f;
 
-// mbarrier slots ([3]/[2] = one per ring slot / S buffer)
+// mbarrier slots
 enum {
-  B_QT = 0,       // Q stored into TMEM (256 softmax threads)
-  B_KFULL = 1,    // K tile landed
-  B_VFULL = 4,    // V tile landed
-  B_KEMPTY = 7,   // S MMA that read the K slot finished
-  B_VEMPTY = 10,  // PV MMA that read the V slot finished
-  B_SFULL = 13,   // S tile in TMEM
-  B_PFULL = 15,   // P tile in TMEM (256 softmax threads)
-  B_PVDONE = 17,  // PV MMA that read the P tile finished (O updated)
-  B_COUNT = 19
+  B_Q = 0,        // Q tile landed
+  B_FULL = 1,     // [PF_RING] ring slot landed
+  B_EMPTY = 1 + PF_RING,        // [PF_RING] MMA that read the slot finished
+  B_SFULL = 1 + 2 * PF_RING,    // [2] S tile in TMEM
+  B_PFULL = 3 + 2 * PF_RING,    // [2] P tile in TMEM (256 softmax threads)
+  B_PVDONE = 5 + 2 * PF_RING,   // [2] PV MMA that read the P tile finished (O updated)
+  B_COUNT = 7 + 2 * PF_RING
 };
+
+// Ring positions: the loads go in the order the MMAs need them,
+// K0, K1, V0, K2, V1, ..., each tile as 4 slots.
+__host__ __device__ constexpr int kpos(int j) { return j == 0 ? 0 : 8 * j - 4; }
+__host__ __device__ constexpr int vpos(int j) { return 8 * (j + 1); }
 
 }  // namespace
 
@@ -135,7 +137,7 @@ __global__ void __launch_bounds__(256) prefill_prologue_kernel(const PrefillPara
     if (is_q) {
       // chunk-major [head][chunk = lane][row]: a warp reading 32 rows of one
       // chunk touches 512 contiguous bytes
-      *reinterpret_cast<uint4*>(p.q_ws + (((size_t)hh * 32 + lane) * PF_MAX_ROWS + r) * 8) = packed;
+      *reinterpret_cast<uint4*>(p.q_ws + ((size_t)hh * PF_MAX_ROWS + r) * HD + lane * 8) = packed;
     } else {
       const size_t out = ((size_t)(hh - QH) * p.capacity + pos) * HD + lane * 8;
       *reinterpret_cast<uint4*>(p.k_cache + out) = packed;
@@ -148,12 +150,14 @@ __global__ void __launch_bounds__(256) prefill_prologue_kernel(const PrefillPara
 
 // Grid: n_qtiles * 24 CTAs, heaviest (last) query tiles first.
 __global__ void __launch_bounds__(PF_THREADS, 1)
-    prefill_attn_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
-                        const PrefillParams p) {
+    prefill_attn_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                        const __grid_constant__ CUtensorMap tv, const PrefillParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + PF_OFF_BAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + B_COUNT);
+  float* xmax = reinterpret_cast<float*>(smem + PF_OFF_BAR + 1024);  // [2 parity][2 half][128 rows]
+  float* xsum = xmax + 2 * 2 * PF_BM;                                  // [2 half][128 rows]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_qt = (p.rows + PF_BM - 1) / PF_BM;
@@ -168,10 +172,10 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
   if (threadIdx.x == 0) p.trace[64 + blockIdx.x * 8 + 0] = global_timer_ns();
 #endif
   if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tq);
     tma_prefetch_desc(&tk);
     tma_prefetch_desc(&tv);
-    for (int b = 0; b < B_COUNT; ++b)
-      mbar_init(&bars[b], (b == B_QT || b == B_PFULL || b == B_PFULL + 1) ? 256 : 1);
+    for (int b = 0; b < B_COUNT; ++b) mbar_init(&bars[b], (b == B_PFULL || b == B_PFULL + 1) ? 256 : 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -205,22 +209,33 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 #endif
 
   if (warp == 0) {
-    // ---------------- TMA producer: K0, K1, V0, K2, V1, ... (need order) ----------------
+    // ---------------- TMA producer ----------------
     if (lane == 0) {
-      auto load = [&](const CUtensorMap* map, int off, int full, int empty, int j) -> bool {
-        const int s = j % PF_KV_STAGES;
-        if (j >= PF_KV_STAGES &&
-            !mbar_wait(&bars[empty + s], ((j / PF_KV_STAGES) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY))
+      mbar_arrive_expect_tx(&bars[B_Q], PF_Q_BYTES);
+      for (int st = 0; st < 4; ++st) tma_load_3d(smem + st * (PF_BM * 128), &tq, &bars[B_Q], st * 64, r0, h);
+      // one ring slot: K sub-tile (keys j*128.., dims 64*part..) or V sub-tile
+      // (keys j*128 + 32*part.., all 256 dims as 4 boxes)
+      auto load_slot = [&](int pos, bool is_k, int j, int part) -> bool {
+        const int slot = pos % PF_RING;
+        if (pos >= PF_RING &&
+            !mbar_wait(&bars[B_EMPTY + slot], ((pos / PF_RING) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY))
           return false;
-        uint8_t* dst = smem + off + s * PF_KV_BYTES;
-        mbar_arrive_expect_tx(&bars[full + s], PF_KV_BYTES);
-        for (int st = 0; st < 4; ++st) tma_load_3d(dst + st * 8192, map, &bars[full + s], st * 64, j * PF_BN, kvh);
+        uint8_t* dst = smem + PF_OFF_RING + slot * PF_SLOT;
+        mbar_arrive_expect_tx(&bars[B_FULL + slot], PF_SLOT);
+        if (is_k) {
+          tma_load_3d(dst, &tk, &bars[B_FULL + slot], part * 64, j * PF_BN, kvh);
+        } else {
+          for (int st = 0; st < 4; ++st)
+            tma_load_3d(dst + st * 4096, &tv, &bars[B_FULL + slot], st * 64, j * PF_BN + part * 32, kvh);
+        }
         return true;
       };
-      bool ok = load(&tk, PF_OFF_K, B_KFULL, B_KEMPTY, 0);
-      for (int i = 1; ok && i <= n_tiles; ++i) {
-        if (i < n_tiles) ok = load(&tk, PF_OFF_K, B_KFULL, B_KEMPTY, i);
-        if (ok) ok = load(&tv, PF_OFF_V, B_VFULL, B_VEMPTY, i - 1);
+      bool ok = true;
+      for (int i = 0; ok && i <= n_tiles; ++i) {
+        if (i < n_tiles)
+          for (int part = 0; ok && part < 4; ++part) ok = load_slot(kpos(i) + part, true, i, part);
+        if (i >= 1)
+          for (int part = 0; ok && part < 4; ++part) ok = load_slot(vpos(i - 1) + part, false, i - 1, part);
       }
     }
     return;
@@ -231,47 +246,56 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     if (lane == 0) {
       constexpr uint32_t IDESC_S = umma_idesc_bf16(PF_BM, PF_BN, false);
       constexpr uint32_t IDESC_O = umma_idesc_bf16(PF_BM, HD, true);
-      bool ok = mbar_wait(&bars[B_QT], 0, p.err, ERR_TIMEOUT_FULL);
+      const uint32_t sQ = smem_u32(smem);
+      const uint32_t sRing = smem_u32(smem + PF_OFF_RING);
+      bool ok = mbar_wait(&bars[B_Q], 0, p.err, ERR_TIMEOUT_FULL);
+      // S_j = Q . K_j^T, 4 K slots (64 dims each) x 4 k-steps of 16
       auto issue_s = [&](int j) -> bool {
-        const int s = j % PF_KV_STAGES, b = j & 1;
-        PT(7);
-        if (!mbar_wait(&bars[B_KFULL + s], (j / PF_KV_STAGES) & 1, p.err, ERR_TIMEOUT_FULL)) return false;
-        PT(0);
-        tc_fence_after();
-        const uint32_t sK = smem_u32(smem + PF_OFF_K + s * PF_KV_BYTES);
-        const uint32_t d = tmem + PF_TMEM_S + b * PF_BN;
+        const uint32_t d = tmem + PF_TMEM_S + (j & 1) * PF_BN;
+        for (int part = 0; part < 4; ++part) {
+          const int pos = kpos(j) + part, slot = pos % PF_RING;
+          PT(7);
+          if (!mbar_wait(&bars[B_FULL + slot], (pos / PF_RING) & 1, p.err, ERR_TIMEOUT_FULL)) return false;
+          PT(0);
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < 16; ++kk) {
-          const uint64_t bd = umma_desc_sw128(sK + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024);
-          umma_bf16_ts(d, tmem + PF_TMEM_Q + kk * 8, bd, IDESC_S, kk > 0);
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t a = umma_desc_sw128(sQ + part * (PF_BM * 128) + kk * 32, 16, 1024);
+            const uint64_t b = umma_desc_sw128(sRing + slot * PF_SLOT + kk * 32, 16, 1024);
+            umma_bf16(d, a, b, IDESC_S, (part | kk) ? 1u : 0u);
+          }
+          umma_commit(&bars[B_EMPTY + slot]);
         }
-        umma_commit(&bars[B_SFULL + b]);
-        umma_commit(&bars[B_KEMPTY + s]);
+        umma_commit(&bars[B_SFULL + (j & 1)]);
         PT(1);
         return true;
       };
-      if (ok) {
-        tc_fence_after();
-        ok = issue_s(0);
-      }
+      if (ok) ok = issue_s(0);
       for (int j = 0; ok && j < n_tiles; ++j) {
-        const int s = j % PF_KV_STAGES, b = j & 1;
+        const int b = j & 1;
         if (j + 1 < n_tiles && !issue_s(j + 1)) break;
         PT(7);
         if (!mbar_wait(&bars[B_PFULL + b], (j >> 1) & 1, p.err, ERR_TIMEOUT_MMA)) break;
         PT(2);
-        if (!mbar_wait(&bars[B_VFULL + s], (j / PF_KV_STAGES) & 1, p.err, ERR_TIMEOUT_FULL)) break;
-        PT(3);
         tc_fence_after();
-        const uint32_t sV = smem_u32(smem + PF_OFF_V + s * PF_KV_BYTES);
+        // O += P_j . V_j: 4 V slots of 32 keys x 2 k-steps; P (bf16 pairs) lives
+        // over the S tile, key k at column k/2
+        for (int part = 0; ok && part < 4; ++part) {
+          const int pos = vpos(j) + part, slot = pos % PF_RING;
+          if (!mbar_wait(&bars[B_FULL + slot], (pos / PF_RING) & 1, p.err, ERR_TIMEOUT_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t bd = umma_desc_sw128(sV + kk * 2048, 8192, 1024);
-          umma_bf16_ts(tmem + PF_TMEM_O, tmem + PF_TMEM_S + b * PF_BN + kk * 8, bd, IDESC_O,
-                       (j > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < 2; ++kk) {
+            const uint64_t bd = umma_desc_sw128(sRing + slot * PF_SLOT + kk * 2048, 4096, 1024);
+            umma_bf16_ts(tmem + PF_TMEM_O, tmem + PF_TMEM_S + b * PF_BN + part * 16 + kk * 8, bd, IDESC_O,
+                         (j > 0 || part > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&bars[B_EMPTY + slot]);
         }
         umma_commit(&bars[B_PVDONE + b]);
-        umma_commit(&bars[B_VEMPTY + s]);
         PT(4);
       }
       PT_FLUSH(0);
@@ -287,33 +311,14 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 
   // ---------------- softmax / correction / epilogue (warps 4..11) ----------------
   // Warp 4+w and warp 8+w share TMEM lanes 32w..32w+31 (one query row per
-  // thread); both take the row max over all 64 scores of a tile, and each
-  // exponentiates, rescales and stores one half of the columns.
+  // thread); each reads and exponentiates one half (64 keys) of a tile, and the
+  // two halves exchange their maxima once per tile.
   const int wi = (warp - 4) & 3;
   const int half = (warp - 4) >> 2;
   const int row = wi * 32 + lane;  // row within the tile == TMEM lane
   const uint32_t lane_addr = tmem + ((uint32_t)(wi * 32) << 16);
   const uint32_t pos_row = p.base + (uint32_t)(r0 + row);
   bool ok = true;
-  {
-    // Q row (bf16) into TMEM columns [384 + 64*half, +64)
-    const uint4* src = reinterpret_cast<const uint4*>(p.q_ws) + ((size_t)h * 32 + half * 16) * PF_MAX_ROWS + r0 + row;
-    uint32_t qa[32], qb[32];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint4 a = src[(size_t)i * PF_MAX_ROWS], b = src[(size_t)(8 + i) * PF_MAX_ROWS];
-      qa[4 * i] = a.x; qa[4 * i + 1] = a.y; qa[4 * i + 2] = a.z; qa[4 * i + 3] = a.w;
-      qb[4 * i] = b.x; qb[4 * i + 1] = b.y; qb[4 * i + 2] = b.z; qb[4 * i + 3] = b.w;
-    }
-    tmem_st32(lane_addr + PF_TMEM_Q + half * 64, qa);
-    tmem_st32(lane_addr + PF_TMEM_Q + half * 64 + 32, qb);
-    tmem_wait_st();
-    tc_fence_before();
-    mbar_arrive(&bars[B_QT]);
-#ifdef LISA_PREFILL_TRACE
-    if (threadIdx.x == 128) p.trace[64 + blockIdx.x * 8 + 2] = global_timer_ns();
-#endif
-  }
   float m2 = -INFINITY, l = 0.f;  // running max (log2 domain), this half's sum
   for (int j = 0; j < n_tiles; ++j) {
     const int b = j & 1;
@@ -325,16 +330,17 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     PT(0);
     tc_fence_after();
     uint32_t sa[32], sb[32];
-    tmem_ld32(lane_addr + PF_TMEM_S + b * PF_BN, sa);
-    tmem_ld32(lane_addr + PF_TMEM_S + b * PF_BN + 32, sb);
+    const uint32_t scol = PF_TMEM_S + b * PF_BN + half * 64;
+    tmem_ld32(lane_addr + scol, sa);
+    tmem_ld32(lane_addr + scol + 32, sb);
     tmem_wait_ld();
-    const uint32_t key0 = (uint32_t)j * PF_BN;
-    const bool full_tile = key0 + PF_BN - 1 <= pos_row;
+    const uint32_t key0 = (uint32_t)j * PF_BN + half * 64;
+    const bool full_half = key0 + 63 <= pos_row;
     float s2[64];
 #pragma unroll
     for (int c = 0; c < 64; ++c) {
       const float raw = __uint_as_float(c < 32 ? sa[c] : sb[c - 32]);
-      s2[c] = (full_tile || key0 + c <= pos_row) ? raw * (SCALE * LOG2E) : -INFINITY;
+      s2[c] = (full_half || key0 + c <= pos_row) ? raw * (SCALE * LOG2E) : -INFINITY;
     }
     float t[32];
 #pragma unroll
@@ -343,24 +349,27 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     for (int w = 16; w >= 1; w >>= 1)
 #pragma unroll
       for (int c = 0; c < w; ++c) t[c] = fmaxf(t[c], t[c + w]);
-    const float mnew = fmaxf(m2, t[0]);
+    xmax[(b * 2 + half) * PF_BM + row] = t[0];
+    // both halves have read this S tile (P overwrites its first 64 columns)
+    // and published their maxima
+    named_bar_sync(2 + wi, 64);
+    const float tmax = fmaxf(t[0], xmax[(b * 2 + (half ^ 1)) * PF_BM + row]);
+    const float mnew = fmaxf(m2, tmax);
     const bool need = mnew > m2 + PF_RESCALE_LOG2;  // also true for the first finite max
     float alpha = 1.f;
     if (need) {
       alpha = fast_exp2(m2 - mnew);
       m2 = mnew;
     }
-    uint32_t pk[16];
-    float ps[16];
+    uint32_t pk[32];
+    float ps[32];
 #pragma unroll
-    for (int c = 0; c < 16; ++c) {
-      const float x0 = half ? s2[32 + 2 * c] : s2[2 * c];
-      const float x1 = half ? s2[33 + 2 * c] : s2[2 * c + 1];
-      pk[c] = pack_bf16x2(fast_exp2(x0 - m2), fast_exp2(x1 - m2));
+    for (int c = 0; c < 32; ++c) {
+      pk[c] = pack_bf16x2(fast_exp2(s2[2 * c] - m2), fast_exp2(s2[2 * c + 1] - m2));
       ps[c] = bf16_bits_to_f32(pk[c] & 0xffffu) + bf16_bits_to_f32(pk[c] >> 16);
     }
 #pragma unroll
-    for (int w = 8; w >= 1; w >>= 1)
+    for (int w = 16; w >= 1; w >>= 1)
 #pragma unroll
       for (int c = 0; c < w; ++c) ps[c] += ps[c + w];
     l = l * alpha + ps[0];
@@ -385,10 +394,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
       tmem_wait_st();
     }
     PT(2);
-    // both halves have read this S tile before P overwrites its first 32 columns
-    named_bar_sync(2 + wi, 64);
-    PT(3);
-    tmem_st16(lane_addr + PF_TMEM_S + b * PF_BN + half * 16, pk);
+    tmem_st32(lane_addr + PF_TMEM_S + b * PF_BN + half * 32, pk);
     tmem_wait_st();
     tc_fence_before();
     mbar_arrive(&bars[B_PFULL + b]);
@@ -413,10 +419,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
   const int last = n_tiles - 1;
   ok = ok && mbar_wait(&bars[B_PVDONE + (last & 1)], (last >> 1) & 1, p.err, ERR_TIMEOUT_MMA);
   // Sum the two halves' denominators (half 0 + half 1).
-  float* lx = reinterpret_cast<float*>(smem + PF_OFF_BAR + 256);
-  lx[half * PF_BM + row] = l;
+  xsum[half * PF_BM + row] = l;
   named_bar_sync(2 + wi, 64);
-  const float l_row = lx[row] + lx[PF_BM + row];
+  const float l_row = xsum[row] + xsum[PF_BM + row];
   if (ok) {
     tc_fence_after();
     const float inv_l = 1.0f / l_row;
@@ -478,16 +483,17 @@ cudaError_t launch_prefill(const PrefillParams& p_in, int num_sms, cudaStream_t 
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  CUtensorMap tk, tv;
+  CUtensorMap tq, tk, tv;
   const uint32_t kv_rows = p.base + (uint32_t)p.rows;
-  if (lisa_encode_kv_map(&tk, p.k_cache, kv_rows, p.capacity, PF_BN, KVH) != 0 ||
-      lisa_encode_kv_map(&tv, p.v_cache, kv_rows, p.capacity, PF_BN, KVH) != 0)
+  if (lisa_encode_kv_map(&tq, p.q_ws, PF_MAX_ROWS, PF_MAX_ROWS, PF_BM, QH) != 0 ||
+      lisa_encode_kv_map(&tk, p.k_cache, kv_rows, p.capacity, PF_BN, KVH) != 0 ||
+      lisa_encode_kv_map(&tv, p.v_cache, kv_rows, p.capacity, 32, KVH) != 0)
     return cudaErrorInvalidValue;
   const int n_qt = (p.rows + PF_BM - 1) / PF_BM;
   cfg.gridDim = dim3(n_qt * QH);
   cfg.blockDim = dim3(PF_THREADS);
   cfg.dynamicSmemBytes = PF_SMEM_BYTES;
-  return cudaLaunchKernelEx(&cfg, prefill_attn_kernel, tk, tv, p);
+  return cudaLaunchKernelEx(&cfg, prefill_attn_kernel, tq, tk, tv, p);
 }
 
 }  // namespace lisa

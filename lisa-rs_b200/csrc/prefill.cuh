@@ -27,7 +27,7 @@ struct PrefillParams {
   uint32_t capacity;
   uint32_t base;      // position of row 0
   int rows;           // 1..512
-  uint16_t* q_ws;     // workspace: normalised query, bf16 [24 heads][32 chunks of 8][512 rows][8]
+  uint16_t* q_ws;     // workspace: normalised query, bf16 [24 heads][512 rows][256]
   uint16_t* gated_out;  // [rows][6144]
   int* err;
   float inv_freq[32];  // filled by launch_prefill
