@@ -85,6 +85,35 @@ __device__ __forceinline__ float fast_rcp(float x) {
   return y;
 }
 
+// Three-input max (sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Packed f32x2 arithmetic (sm_100): one instruction for two lanes of work.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  uint64_t d;
+  asm("{\n\t.reg .b64 ra, rb, rc;\n\tmov.b64 ra, {%1, %2};\n\tmov.b64 rb, {%3, %4};\n\t"
+      "mov.b64 rc, {%5, %6};\n\tfma.rn.f32x2 %0, ra, rb, rc;\n\t}"
+      : "=l"(d)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return make_float2(__uint_as_float((uint32_t)d), __uint_as_float((uint32_t)(d >> 32)));
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  uint64_t d;
+  asm("{\n\t.reg .b64 ra, rb;\n\tmov.b64 ra, {%1, %2};\n\tmov.b64 rb, {%3, %4};\n\t"
+      "add.rn.f32x2 %0, ra, rb;\n\t}"
+      : "=l"(d)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return make_float2(__uint_as_float((uint32_t)d), __uint_as_float((uint32_t)(d >> 32)));
+}
+// The two bf16 halves of a packed word as f32 (exact).
+__device__ __forceinline__ float2 unpack_bf16x2(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+
 __device__ __forceinline__ uint64_t global_timer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -33,35 +33,37 @@ namespace lisa {
 
 namespace {
 
-constexpr int PF_BM = 128;   // query rows per CTA
-constexpr int PF_BN = 128;   // keys per tile
-constexpr int PF_SLOT = 16384;  // ring slot: K sub-tile [128 keys][64 dims] or V sub-tile [32 keys][256 dims]
-constexpr int PF_RING = 9;
-constexpr int PF_Q_BYTES = PF_BM * HD * 2;  // 64 KB
-constexpr int PF_OFF_RING = PF_Q_BYTES;
-constexpr int PF_OFF_BAR = PF_OFF_RING + PF_RING * PF_SLOT;
+constexpr int PF_BM = 128;        // query rows per CTA (TMEM lanes)
+constexpr int PF_BN = 128;        // keys per tile
+constexpr int PF_Q_BYTES = PF_BM * HD * 2;          // 64 KB: this CTA's 128 query rows
+constexpr int PF_KH_BYTES = (PF_BN / 2) * HD * 2;   // 32 KB: this CTA's 64 keys of a K tile
+constexpr int PF_VH_BYTES = PF_BN * (HD / 2) * 2;   // 32 KB: this CTA's 128 dims of a V tile
+constexpr int PF_OFF_K = PF_Q_BYTES;                // 2 K slots
+constexpr int PF_OFF_V = PF_OFF_K + 2 * PF_KH_BYTES;  // 2 V slots
+constexpr int PF_OFF_BAR = PF_OFF_V + 2 * PF_VH_BYTES;
 constexpr int PF_SMEM_BYTES = PF_OFF_BAR + 4096 + 1024;  // barriers, TMEM slot, max/sum exchange
-constexpr int PF_THREADS = 384;  // warp 0 TMA, warp 1 MMA, warps 4..11 softmax
+constexpr int PF_THREADS = 384;  // warp 0 Q/K loads, 1 MMA, 2 V loads, 4..11 softmax
 constexpr uint32_t PF_TMEM_COLS = 512;
 constexpr uint32_t PF_TMEM_O = 0;    // O accumulator: columns [0, 256)
 constexpr uint32_t PF_TMEM_S = 256;  // S / P tiles: columns [256, 384), [384, 512)
 constexpr float PF_RESCALE_LOG2 = 8.0f;
+constexpr float kLog2Scale = SCALE * LOG2E;  // raw score -> exp2 argument
+constexpr uint16_t PF_PAIR = 3;  // multicast mask: both CTAs of the pair
 
-// mbarrier slots
+// mbarrier slots. *FULL, Q and PFULL are waited on by the pair's MMA issuer
+// (rank 0) and complete with both CTAs' loads / arrivals; *EMPTY, SFULL and
+// PVDONE are signalled to both CTAs by the MMA commits.
 enum {
-  B_Q = 0,        // Q tile landed
-  B_FULL = 1,     // [PF_RING] ring slot landed
-  B_EMPTY = 1 + PF_RING,        // [PF_RING] MMA that read the slot finished
-  B_SFULL = 1 + 2 * PF_RING,    // [2] S tile in TMEM
-  B_PFULL = 3 + 2 * PF_RING,    // [2] P tile in TMEM (256 softmax threads)
-  B_PVDONE = 5 + 2 * PF_RING,   // [2] PV MMA that read the P tile finished (O updated)
-  B_COUNT = 7 + 2 * PF_RING
+  B_Q = 0,
+  B_KFULL = 1,    // [2]
+  B_KEMPTY = 3,   // [2]
+  B_VFULL = 5,    // [2]
+  B_VEMPTY = 7,   // [2]
+  B_SFULL = 9,    // [2] S tile in TMEM
+  B_PFULL = 11,   // [2] P tile in TMEM (8 softmax warps x 2 CTAs)
+  B_PVDONE = 13,  // [2] P.V MMA that read the P tile finished (O updated)
+  B_COUNT = 15
 };
-
-// Ring positions: the loads go in the order the MMAs need them,
-// K0, K1, V0, K2, V1, ..., each tile as 4 slots.
-__host__ __device__ constexpr int kpos(int j) { return j == 0 ? 0 : 8 * j - 4; }
-__host__ __device__ constexpr int vpos(int j) { return 8 * (j + 1); }
 
 }  // namespace
 
@@ -148,8 +150,10 @@ __global__ void __launch_bounds__(256) prefill_prologue_kernel(const PrefillPara
   }
 }
 
-// Grid: n_qtiles * 24 CTAs, heaviest (last) query tiles first.
-__global__ void __launch_bounds__(PF_THREADS, 1)
+// Grid: clusters of 2 CTAs, n_pairs * 24 clusters, heaviest (last) query
+// row pairs first. Cluster rank 0 holds query rows [256 qp, 256 qp + 128),
+// rank 1 the next 128.
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
     prefill_attn_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                         const __grid_constant__ CUtensorMap tv, const PrefillParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -160,12 +164,15 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
   float* xsum = xmax + 2 * 2 * PF_BM;                                  // [2 half][128 rows]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
   const int n_qt = (p.rows + PF_BM - 1) / PF_BM;
-  const int qt = n_qt - 1 - (int)(blockIdx.x / QH);
-  const int h = blockIdx.x % QH, kvh = h / GQA;
-  const int r0 = qt * PF_BM;
-  const int r_end = min(r0 + PF_BM, p.rows);
-  const uint32_t kv_end = p.base + (uint32_t)r_end;  // keys [0, kv_end)
+  const int n_pairs = (n_qt + 1) / 2;
+  const int cl = (int)(blockIdx.x >> 1);
+  const int qp = n_pairs - 1 - cl / QH;
+  const int h = cl % QH, kvh = h / GQA;
+  const int r0 = qp * 2 * PF_BM + (int)rank * PF_BM;
+  const int pair_end = min(qp * 2 * PF_BM + 2 * PF_BM, p.rows);
+  const uint32_t kv_end = p.base + (uint32_t)pair_end;  // keys [0, kv_end) for both CTAs
   const int n_tiles = (int)((kv_end + PF_BN - 1) / PF_BN);
 
 #ifdef LISA_PREFILL_TRACE
@@ -175,17 +182,20 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     tma_prefetch_desc(&tq);
     tma_prefetch_desc(&tk);
     tma_prefetch_desc(&tv);
-    for (int b = 0; b < B_COUNT; ++b) mbar_init(&bars[b], (b == B_PFULL || b == B_PFULL + 1) ? 256 : 1);
+    for (int b = 0; b < B_COUNT; ++b) mbar_init(&bars[b], (b == B_PFULL || b == B_PFULL + 1) ? 16 : 1);
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, PF_TMEM_COLS);
-    tmem_relinquish();
+    tmem_alloc_pair(tmem_slot, PF_TMEM_COLS);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // shared::cluster address of rank 0's barrier `i`
+  const uint32_t lead_bars = cluster_map(smem_u32(bars), 0);
+  auto lead_bar = [&](int i) -> uint32_t { return lead_bars + 8u * (uint32_t)i; };
   // Setup above overlaps the prologue kernel; its q_ws / KV writes are read
   // only after it has completed.
   pdl_wait_primary();
@@ -208,256 +218,249 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 #define PT_FLUSH(role)
 #endif
 
-  if (warp == 0) {
-    // ---------------- TMA producer ----------------
-    if (lane == 0) {
-      mbar_arrive_expect_tx(&bars[B_Q], PF_Q_BYTES);
-      for (int st = 0; st < 4; ++st) tma_load_3d(smem + st * (PF_BM * 128), &tq, &bars[B_Q], st * 64, r0, h);
-      // one ring slot: K sub-tile (keys j*128.., dims 64*part..) or V sub-tile
-      // (keys j*128 + 32*part.., all 256 dims as 4 boxes)
-      auto load_slot = [&](int pos, bool is_k, int j, int part) -> bool {
-        const int slot = pos % PF_RING;
-        if (pos >= PF_RING &&
-            !mbar_wait(&bars[B_EMPTY + slot], ((pos / PF_RING) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY))
-          return false;
-        uint8_t* dst = smem + PF_OFF_RING + slot * PF_SLOT;
-        mbar_arrive_expect_tx(&bars[B_FULL + slot], PF_SLOT);
-        if (is_k) {
-          tma_load_3d(dst, &tk, &bars[B_FULL + slot], part * 64, j * PF_BN, kvh);
-        } else {
-          for (int st = 0; st < 4; ++st)
-            tma_load_3d(dst + st * 4096, &tv, &bars[B_FULL + slot], st * 64, j * PF_BN + part * 32, kvh);
-        }
-        return true;
-      };
-      bool ok = true;
-      for (int i = 0; ok && i <= n_tiles; ++i) {
-        if (i < n_tiles)
-          for (int part = 0; ok && part < 4; ++part) ok = load_slot(kpos(i) + part, true, i, part);
-        if (i >= 1)
-          for (int part = 0; ok && part < 4; ++part) ok = load_slot(vpos(i - 1) + part, false, i - 1, part);
+  if (warp == 0 && lane == 0) {
+    // ---------------- Q and K loads ----------------
+    // Each CTA loads its own 128 query rows and its half (64 keys) of every
+    // K tile; completion is counted on rank 0's barriers, whose expected
+    // byte count rank 0 sets for both.
+    if (rank == 0) mbar_arrive_expect_tx(&bars[B_Q], 2 * PF_Q_BYTES);
+    tma_load_4d_pair(smem, &tq, lead_bar(B_Q), 0, r0, 0, h);
+    for (int j = 0; j < n_tiles; ++j) {
+      const int s = j & 1;
+      if (j >= 2 && !mbar_wait(&bars[B_KEMPTY + s], ((j >> 1) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) break;
+      if (rank == 0) mbar_arrive_expect_tx(&bars[B_KFULL + s], 2 * PF_KH_BYTES);
+      tma_load_4d_pair(smem + PF_OFF_K + s * PF_KH_BYTES, &tk, lead_bar(B_KFULL + s), 0,
+                       j * PF_BN + (int)rank * (PF_BN / 2), 0, kvh);
+    }
+  } else if (warp == 2 && lane == 0) {
+    // ---------------- V loads: this CTA's 128 dims of every V tile ----------------
+    for (int j = 0; j < n_tiles; ++j) {
+      const int s = j & 1;
+      if (j >= 2 && !mbar_wait(&bars[B_VEMPTY + s], ((j >> 1) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) break;
+      if (rank == 0) mbar_arrive_expect_tx(&bars[B_VFULL + s], 2 * PF_VH_BYTES);
+      tma_load_4d_pair(smem + PF_OFF_V + s * PF_VH_BYTES, &tv, lead_bar(B_VFULL + s), 0, j * PF_BN,
+                       2 * (int)rank, kvh);
+    }
+  } else if (warp == 1 && lane == 0 && rank == 0) {
+    // ---------------- MMA issuer (rank 0 only, M = 256 over the pair) ----------------
+    constexpr uint32_t IDESC_S = umma_idesc_bf16(2 * PF_BM, PF_BN, false);
+    constexpr uint32_t IDESC_O = umma_idesc_bf16(2 * PF_BM, HD, true);
+    const uint32_t sQ = smem_u32(smem);
+    const uint32_t sK = smem_u32(smem + PF_OFF_K);
+    const uint32_t sV = smem_u32(smem + PF_OFF_V);
+    bool ok = mbar_wait(&bars[B_Q], 0, p.err, ERR_TIMEOUT_FULL);
+    // S_j = Q . K_j^T: 16 k-steps of 16 dims; Q rows and K keys are stored as
+    // [64-dim group][row][64 dims]
+    auto issue_s = [&](int j) -> bool {
+      const int s = j & 1;
+      PT(7);
+      if (!mbar_wait(&bars[B_KFULL + s], (j >> 1) & 1, p.err, ERR_TIMEOUT_FULL)) return false;
+      PT(0);
+      tc_fence_after();
+      const uint32_t d = tmem + PF_TMEM_S + (uint32_t)s * PF_BN;
+#pragma unroll
+      for (int kk = 0; kk < 16; ++kk) {
+        const uint32_t g = kk >> 2, sub = kk & 3;
+        const uint64_t a = umma_desc_sw128(sQ + g * (PF_BM * 128) + sub * 32, 16, 1024);
+        const uint64_t b = umma_desc_sw128(sK + s * PF_KH_BYTES + g * ((PF_BN / 2) * 128) + sub * 32, 16, 1024);
+        umma_pair_bf16(d, a, b, IDESC_S, kk ? 1u : 0u);
       }
-    }
-    return;
-  }
-
-  if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      constexpr uint32_t IDESC_S = umma_idesc_bf16(PF_BM, PF_BN, false);
-      constexpr uint32_t IDESC_O = umma_idesc_bf16(PF_BM, HD, true);
-      const uint32_t sQ = smem_u32(smem);
-      const uint32_t sRing = smem_u32(smem + PF_OFF_RING);
-      bool ok = mbar_wait(&bars[B_Q], 0, p.err, ERR_TIMEOUT_FULL);
-      // S_j = Q . K_j^T, 4 K slots (64 dims each) x 4 k-steps of 16
-      auto issue_s = [&](int j) -> bool {
-        const uint32_t d = tmem + PF_TMEM_S + (j & 1) * PF_BN;
-        for (int part = 0; part < 4; ++part) {
-          const int pos = kpos(j) + part, slot = pos % PF_RING;
-          PT(7);
-          if (!mbar_wait(&bars[B_FULL + slot], (pos / PF_RING) & 1, p.err, ERR_TIMEOUT_FULL)) return false;
-          PT(0);
-          tc_fence_after();
+      umma_pair_commit(&bars[B_KEMPTY + s], PF_PAIR);
+      umma_pair_commit(&bars[B_SFULL + s], PF_PAIR);
+      PT(1);
+      return true;
+    };
+    if (ok) ok = issue_s(0);
+    for (int j = 0; ok && j < n_tiles; ++j) {
+      const int b = j & 1;
+      if (j + 1 < n_tiles && !issue_s(j + 1)) break;
+      PT(7);
+      if (!mbar_wait(&bars[B_PFULL + b], (j >> 1) & 1, p.err, ERR_TIMEOUT_MMA)) break;
+      PT(2);
+      if (!mbar_wait(&bars[B_VFULL + b], (j >> 1) & 1, p.err, ERR_TIMEOUT_FULL)) break;
+      PT(3);
+      tc_fence_after();
+      // O += P_j . V_j: 8 k-steps of 16 keys; P (bf16 pairs) lives over the S
+      // tile, key k at column k/2; V is stored [64-dim group][key][64 dims]
+      // and read MN-major (this CTA holds 2 of the 4 groups)
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t a = umma_desc_sw128(sQ + part * (PF_BM * 128) + kk * 32, 16, 1024);
-            const uint64_t b = umma_desc_sw128(sRing + slot * PF_SLOT + kk * 32, 16, 1024);
-            umma_bf16(d, a, b, IDESC_S, (part | kk) ? 1u : 0u);
-          }
-          umma_commit(&bars[B_EMPTY + slot]);
-        }
-        umma_commit(&bars[B_SFULL + (j & 1)]);
-        PT(1);
-        return true;
-      };
-      if (ok) ok = issue_s(0);
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        const int b = j & 1;
-        if (j + 1 < n_tiles && !issue_s(j + 1)) break;
-        PT(7);
-        if (!mbar_wait(&bars[B_PFULL + b], (j >> 1) & 1, p.err, ERR_TIMEOUT_MMA)) break;
-        PT(2);
-        tc_fence_after();
-        // O += P_j . V_j: 4 V slots of 32 keys x 2 k-steps; P (bf16 pairs) lives
-        // over the S tile, key k at column k/2
-        for (int part = 0; ok && part < 4; ++part) {
-          const int pos = vpos(j) + part, slot = pos % PF_RING;
-          if (!mbar_wait(&bars[B_FULL + slot], (pos / PF_RING) & 1, p.err, ERR_TIMEOUT_FULL)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < 2; ++kk) {
-            const uint64_t bd = umma_desc_sw128(sRing + slot * PF_SLOT + kk * 2048, 4096, 1024);
-            umma_bf16_ts(tmem + PF_TMEM_O, tmem + PF_TMEM_S + b * PF_BN + part * 16 + kk * 8, bd, IDESC_O,
-                         (j > 0 || part > 0 || kk > 0) ? 1u : 0u);
-          }
-          umma_commit(&bars[B_EMPTY + slot]);
-        }
-        umma_commit(&bars[B_PVDONE + b]);
-        PT(4);
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint64_t bd = umma_desc_sw128(sV + b * PF_VH_BYTES + kk * 2048, PF_BN * 128, 1024);
+        umma_pair_bf16_ts(tmem + PF_TMEM_O, tmem + PF_TMEM_S + b * PF_BN + kk * 8, bd, IDESC_O,
+                          (j > 0 || kk > 0) ? 1u : 0u);
       }
-      PT_FLUSH(0);
+      umma_pair_commit(&bars[B_VEMPTY + b], PF_PAIR);
+      umma_pair_commit(&bars[B_PVDONE + b], PF_PAIR);
+      PT(4);
     }
-    __syncwarp();
-    named_bar_sync(1, 288);
-    tc_fence_after();
-    tmem_dealloc(tmem, PF_TMEM_COLS);
-    return;
+    PT_FLUSH(0);
   }
-
-  if (warp < 4) return;
-
-  // ---------------- softmax / correction / epilogue (warps 4..11) ----------------
-  // Warp 4+w and warp 8+w share TMEM lanes 32w..32w+31 (one query row per
-  // thread); each reads and exponentiates one half (64 keys) of a tile, and the
-  // two halves exchange their maxima once per tile.
-  const int wi = (warp - 4) & 3;
-  const int half = (warp - 4) >> 2;
-  const int row = wi * 32 + lane;  // row within the tile == TMEM lane
-  const uint32_t lane_addr = tmem + ((uint32_t)(wi * 32) << 16);
-  const uint32_t pos_row = p.base + (uint32_t)(r0 + row);
-  bool ok = true;
-  float m2 = -INFINITY, l = 0.f;  // running max (log2 domain), this half's sum
-  for (int j = 0; j < n_tiles; ++j) {
-    const int b = j & 1;
-    PT(7);
-    if (!mbar_wait(&bars[B_SFULL + b], (j >> 1) & 1, p.err, ERR_TIMEOUT_MMA)) {
-      ok = false;
-      break;
-    }
-    PT(0);
-    tc_fence_after();
-    uint32_t sa[32], sb[32];
-    const uint32_t scol = PF_TMEM_S + b * PF_BN + half * 64;
-    tmem_ld32(lane_addr + scol, sa);
-    tmem_ld32(lane_addr + scol + 32, sb);
-    tmem_wait_ld();
-    const uint32_t key0 = (uint32_t)j * PF_BN + half * 64;
-    const bool full_half = key0 + 63 <= pos_row;
-    float s2[64];
-#pragma unroll
-    for (int c = 0; c < 64; ++c) {
-      const float raw = __uint_as_float(c < 32 ? sa[c] : sb[c - 32]);
-      s2[c] = (full_half || key0 + c <= pos_row) ? raw * (SCALE * LOG2E) : -INFINITY;
-    }
-    float t[32];
-#pragma unroll
-    for (int c = 0; c < 32; ++c) t[c] = fmaxf(s2[c], s2[c + 32]);
-#pragma unroll
-    for (int w = 16; w >= 1; w >>= 1)
-#pragma unroll
-      for (int c = 0; c < w; ++c) t[c] = fmaxf(t[c], t[c + w]);
-    xmax[(b * 2 + half) * PF_BM + row] = t[0];
-    // both halves have read this S tile (P overwrites its first 64 columns)
-    // and published their maxima
-    named_bar_sync(2 + wi, 64);
-    const float tmax = fmaxf(t[0], xmax[(b * 2 + (half ^ 1)) * PF_BM + row]);
-    const float mnew = fmaxf(m2, tmax);
-    const bool need = mnew > m2 + PF_RESCALE_LOG2;  // also true for the first finite max
-    float alpha = 1.f;
-    if (need) {
-      alpha = fast_exp2(m2 - mnew);
-      m2 = mnew;
-    }
-    uint32_t pk[32];
-    float ps[32];
-#pragma unroll
-    for (int c = 0; c < 32; ++c) {
-      pk[c] = pack_bf16x2(fast_exp2(s2[2 * c] - m2), fast_exp2(s2[2 * c + 1] - m2));
-      ps[c] = bf16_bits_to_f32(pk[c] & 0xffffu) + bf16_bits_to_f32(pk[c] >> 16);
-    }
-#pragma unroll
-    for (int w = 16; w >= 1; w >>= 1)
-#pragma unroll
-      for (int c = 0; c < w; ++c) ps[c] += ps[c + w];
-    l = l * alpha + ps[0];
-    PT(1);
-    if (j > 0 && __any_sync(0xffffffffu, need)) {
-      // O must hold exactly tiles < j before it is rescaled
-      if (!mbar_wait(&bars[B_PVDONE + (b ^ 1)], ((j - 1) >> 1) & 1, p.err, ERR_TIMEOUT_MMA)) {
+  else if (warp >= 4) {
+    // ---------------- softmax / correction / epilogue (warps 4..11) ----------------
+    // Warp 4+w and warp 8+w share TMEM lanes 32w..32w+31 (one query row per
+    // thread); each reads and exponentiates one half (64 keys) of a tile, and
+    // the two halves exchange their maxima once per tile.
+    const int wi = (warp - 4) & 3;
+    const int half = (warp - 4) >> 2;
+    const int row = wi * 32 + lane;  // row within the CTA's tile == TMEM lane
+    const uint32_t lane_addr = tmem + ((uint32_t)(wi * 32) << 16);
+    const uint32_t pos_row = p.base + (uint32_t)(r0 + row);
+    bool ok = true;
+    float mr = -INFINITY, l = 0.f;  // running max of the raw scores, this half's sum
+    for (int j = 0; j < n_tiles; ++j) {
+      const int b = j & 1;
+      PT(7);
+      if (!mbar_wait(&bars[B_SFULL + b], (j >> 1) & 1, p.err, ERR_TIMEOUT_MMA)) {
         ok = false;
         break;
       }
+      PT(0);
       tc_fence_after();
-#pragma unroll 1
-      for (int c = 0; c < HD / 64; ++c) {
-        const uint32_t col = PF_TMEM_O + half * (HD / 2) + c * 32;
-        uint32_t ov[32];
-        tmem_ld32(lane_addr + col, ov);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
-        tmem_st32(lane_addr + col, ov);
-      }
-      tmem_wait_st();
-    }
-    PT(2);
-    tmem_st32(lane_addr + PF_TMEM_S + b * PF_BN + half * 32, pk);
-    tmem_wait_st();
-    tc_fence_before();
-    mbar_arrive(&bars[B_PFULL + b]);
-    PT(4);
-  }
-#ifdef LISA_PREFILL_TRACE
-  if (threadIdx.x == 128) p.trace[64 + blockIdx.x * 8 + 3] = global_timer_ns();
-#endif
-  // gate values of this row and half, prefetched while the last P.V runs
-  const int r = r0 + row;
-  uint32_t gpk[64];
-  if (ok && r < p.rows) {
-    const size_t gbase = (size_t)r * QROW + (size_t)h * 512 + 256 + half * 128;
-#pragma unroll
-    for (int g8 = 0; g8 < 16; ++g8) {
-      float gv[8];
-      load8_in(p.q_gate, gbase + g8 * 8, p.in_bf16, gv);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) gpk[g8 * 4 + i] = pack_bf16x2(gv[2 * i], gv[2 * i + 1]);
-    }
-  }
-  const int last = n_tiles - 1;
-  ok = ok && mbar_wait(&bars[B_PVDONE + (last & 1)], (last >> 1) & 1, p.err, ERR_TIMEOUT_MMA);
-  // Sum the two halves' denominators (half 0 + half 1).
-  xsum[half * PF_BM + row] = l;
-  named_bar_sync(2 + wi, 64);
-  const float l_row = xsum[row] + xsum[PF_BM + row];
-  if (ok) {
-    tc_fence_after();
-    const float inv_l = 1.0f / l_row;
-#pragma unroll
-    for (int c = 0; c < HD / 64; ++c) {
-      const int col = half * (HD / 2) + c * 32;
-      uint32_t ov[32];
-      tmem_ld32(lane_addr + PF_TMEM_O + col, ov);
+      uint32_t sa[32], sb[32];
+      const uint32_t scol = PF_TMEM_S + b * PF_BN + half * 64;
+      tmem_ld32(lane_addr + scol, sa);
+      tmem_ld32(lane_addr + scol + 32, sb);
       tmem_wait_ld();
-      if (r < p.rows) {
-        uint32_t outw[16];
+      float x[64];  // raw scores Q.K (unscaled)
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const uint32_t gg = gpk[c * 16 + i];
-          float y[2];
+      for (int c = 0; c < 64; ++c) x[c] = __uint_as_float(c < 32 ? sa[c] : sb[c - 32]);
+      const uint32_t key0 = (uint32_t)j * PF_BN + half * 64;
+      if (key0 + 63 > pos_row) {  // diagonal tile: keys past this row's position
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const float gv = bf16_bits_to_f32(e ? gg >> 16 : gg & 0xffffu);
-            const float sg = fast_rcp(1.0f + fast_exp2(-LOG2E * gv));
-            y[e] = __uint_as_float(ov[2 * i + e]) * inv_l * sg;
-          }
-          outw[i] = pack_bf16x2(y[0], y[1]);
+        for (int c = 0; c < 64; ++c)
+          if (key0 + c > pos_row) x[c] = -INFINITY;
+      }
+      float t8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        t8[i] = fmaxf(fmax3(fmax3(x[8 * i], x[8 * i + 1], x[8 * i + 2]), x[8 * i + 3], x[8 * i + 4]),
+                      fmax3(x[8 * i + 5], x[8 * i + 6], x[8 * i + 7]));
+      const float hmax = fmax3(fmax3(t8[0], t8[1], t8[2]), fmax3(t8[3], t8[4], t8[5]), fmaxf(t8[6], t8[7]));
+      xmax[(b * 2 + half) * PF_BM + row] = hmax;
+      // both halves have read this S tile (P overwrites its first 64 columns)
+      // and published their maxima
+      named_bar_sync(2 + wi, 64);
+      const float mnew = fmax3(mr, hmax, xmax[(b * 2 + (half ^ 1)) * PF_BM + row]);
+      // the running max moves only when it grows by more than 2^8 (in exp2 units)
+      const bool need = (mnew - mr) * kLog2Scale > PF_RESCALE_LOG2;  // also true for the first finite max
+      float alpha = 1.f;
+      if (need) {
+        alpha = fast_exp2((mr - mnew) * kLog2Scale);
+        mr = mnew;
+      }
+      // P = exp2(x * scale*log2e - m), rounded to bf16 and written over the S
+      // tile 16 keys at a time so the TMEM stores overlap the exponentials;
+      // the denominator sums the rounded values the P.V MMA uses.
+      const float2 cc = make_float2(kLog2Scale, kLog2Scale);
+      const float2 nm = make_float2(-mr * kLog2Scale, -mr * kLog2Scale);
+      float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t pk[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const float2 e = ffma2(make_float2(x[16 * q + 2 * c], x[16 * q + 2 * c + 1]), cc, nm);
+          pk[c] = pack_bf16x2(fast_exp2(e.x), fast_exp2(e.y));
+          if (c & 1) acc1 = fadd2(acc1, unpack_bf16x2(pk[c]));
+          else acc0 = fadd2(acc0, unpack_bf16x2(pk[c]));
         }
-        uint4* dst = reinterpret_cast<uint4*>(p.gated_out + (size_t)r * OROW + h * HD + col);
+        tmem_st8(lane_addr + PF_TMEM_S + b * PF_BN + half * 32 + q * 8, pk);
+      }
+      const float2 acc = fadd2(acc0, acc1);
+      l = l * alpha + (acc.x + acc.y);
+      PT(1);
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        // O must hold exactly tiles < j before it is rescaled
+        if (!mbar_wait(&bars[B_PVDONE + (b ^ 1)], ((j - 1) >> 1) & 1, p.err, ERR_TIMEOUT_MMA)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < HD / 64; ++c) {
+          const uint32_t col = PF_TMEM_O + half * (HD / 2) + c * 32;
+          uint32_t ov[32];
+          tmem_ld32(lane_addr + col, ov);
+          tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 4; ++i) dst[i] = make_uint4(outw[4 * i], outw[4 * i + 1], outw[4 * i + 2], outw[4 * i + 3]);
+          for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+          tmem_st32(lane_addr + col, ov);
+        }
+      }
+      PT(2);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster_relaxed(lead_bar(B_PFULL + b));
+      PT(4);
+    }
+#ifdef LISA_PREFILL_TRACE
+    if (threadIdx.x == 128) p.trace[64 + blockIdx.x * 8 + 3] = global_timer_ns();
+#endif
+    // gate values of this row and half, prefetched while the last P.V runs
+    const int r = r0 + row;
+    uint32_t gpk[64];
+    if (ok && r < p.rows) {
+      const size_t gbase = (size_t)r * QROW + (size_t)h * 512 + 256 + half * 128;
+#pragma unroll
+      for (int g8 = 0; g8 < 16; ++g8) {
+        float gv[8];
+        load8_in(p.q_gate, gbase + g8 * 8, p.in_bf16, gv);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) gpk[g8 * 4 + i] = pack_bf16x2(gv[2 * i], gv[2 * i + 1]);
       }
     }
-  }
-  PT(5);
-  if (warp == 4) { PT_FLUSH(1); }
+    const int last = n_tiles - 1;
+    ok = ok && mbar_wait(&bars[B_PVDONE + (last & 1)], (last >> 1) & 1, p.err, ERR_TIMEOUT_MMA);
+    // Sum the two halves' denominators (half 0 + half 1).
+    xsum[half * PF_BM + row] = l;
+    named_bar_sync(2 + wi, 64);
+    const float l_row = xsum[row] + xsum[PF_BM + row];
+    if (ok) {
+      tc_fence_after();
+      const float inv_l = 1.0f / l_row;
+#pragma unroll
+      for (int c = 0; c < HD / 64; ++c) {
+        const int col = half * (HD / 2) + c * 32;
+        uint32_t ov[32];
+        tmem_ld32(lane_addr + PF_TMEM_O + col, ov);
+        tmem_wait_ld();
+        if (r < p.rows) {
+          uint32_t outw[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const uint32_t gg = gpk[c * 16 + i];
+            float y[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const float gv = bf16_bits_to_f32(e ? gg >> 16 : gg & 0xffffu);
+              const float sg = fast_rcp(1.0f + fast_exp2(-LOG2E * gv));
+              y[e] = __uint_as_float(ov[2 * i + e]) * inv_l * sg;
+            }
+            outw[i] = pack_bf16x2(y[0], y[1]);
+          }
+          uint4* dst = reinterpret_cast<uint4*>(p.gated_out + (size_t)r * OROW + h * HD + col);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            dst[i] = make_uint4(outw[4 * i], outw[4 * i + 1], outw[4 * i + 2], outw[4 * i + 3]);
+        }
+      }
+    }
+    PT(5);
+    if (warp == 4) { PT_FLUSH(1); }
 #ifdef LISA_PREFILL_TRACE
-  if (threadIdx.x == 128) p.trace[64 + blockIdx.x * 8 + 4] = global_timer_ns();
+    if (threadIdx.x == 128) p.trace[64 + blockIdx.x * 8 + 4] = global_timer_ns();
 #endif
+  }
+  // Both CTAs are done with TMEM and with each other's barriers before either
+  // frees its columns or exits.
+  __syncwarp();
   tc_fence_before();
-  named_bar_sync(1, 288);
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, PF_TMEM_COLS);
+  }
 }
 
 size_t prefill_workspace_bytes() { return (size_t)QH * PF_MAX_ROWS * HD * sizeof(uint16_t); }
@@ -485,12 +488,13 @@ cudaError_t launch_prefill(const PrefillParams& p_in, int num_sms, cudaStream_t 
   }
   CUtensorMap tq, tk, tv;
   const uint32_t kv_rows = p.base + (uint32_t)p.rows;
-  if (lisa_encode_kv_map(&tq, p.q_ws, PF_MAX_ROWS, PF_MAX_ROWS, PF_BM, QH) != 0 ||
-      lisa_encode_kv_map(&tk, p.k_cache, kv_rows, p.capacity, PF_BN, KVH) != 0 ||
-      lisa_encode_kv_map(&tv, p.v_cache, kv_rows, p.capacity, 32, KVH) != 0)
+  if (lisa_encode_group_map(&tq, p.q_ws, PF_MAX_ROWS, PF_MAX_ROWS, QH, PF_BM, 4) != 0 ||
+      lisa_encode_group_map(&tk, p.k_cache, kv_rows, p.capacity, KVH, PF_BN / 2, 4) != 0 ||
+      lisa_encode_group_map(&tv, p.v_cache, kv_rows, p.capacity, KVH, PF_BN, 2) != 0)
     return cudaErrorInvalidValue;
   const int n_qt = (p.rows + PF_BM - 1) / PF_BM;
-  cfg.gridDim = dim3(n_qt * QH);
+  const int n_pairs = (n_qt + 1) / 2;
+  cfg.gridDim = dim3(n_pairs * QH * 2);
   cfg.blockDim = dim3(PF_THREADS);
   cfg.dynamicSmemBytes = PF_SMEM_BYTES;
   return cudaLaunchKernelEx(&cfg, prefill_attn_kernel, tq, tk, tv, p);

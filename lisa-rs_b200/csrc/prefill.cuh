@@ -9,6 +9,10 @@
 // SWIZZLE_128B. Defined in runtime.cu.
 int lisa_encode_kv_map(CUtensorMap* map, const void* base, uint32_t rows, uint32_t window_rows, uint32_t box_rows,
                        uint32_t planes);
+// The same array seen as 64-dim groups: dims {64, rows, 4, planes}, boxes
+// {64, box_rows, box_groups, 1} landing as [group][row][64]. Defined in runtime.cu.
+int lisa_encode_group_map(CUtensorMap* map, const void* base, uint32_t rows, uint32_t window_rows, uint32_t planes,
+                          uint32_t box_rows, uint32_t box_groups);
 
 namespace lisa {
 

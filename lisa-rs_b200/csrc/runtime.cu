@@ -78,6 +78,25 @@ int lisa_encode_kv_map(CUtensorMap* map, const void* base, uint32_t rows, uint32
   return r == CUDA_SUCCESS ? LISA_OK : LISA_ECUDA;
 }
 
+// Tensor map over a bf16 [planes][window_rows][256] array seen as 64-dim
+// groups: dims {64, rows, 4 groups, planes} (strides 512 B, 128 B,
+// window_rows * 512 B); boxes {64, box_rows, box_groups, 1} with 128-byte
+// swizzle land in shared memory as [group][row][64 dims], one 128-byte row per
+// (group, row); positions >= rows read as zero.
+int lisa_encode_group_map(CUtensorMap* map, const void* base, uint32_t rows, uint32_t window_rows, uint32_t planes,
+                          uint32_t box_rows, uint32_t box_groups) {
+  auto enc = get_encode();
+  if (!enc) return LISA_ECUDA;
+  cuuint64_t dims[4] = {64, rows, 4, planes};
+  cuuint64_t strides[3] = {512, 128, (cuuint64_t)window_rows * 512};
+  cuuint32_t box[4] = {64, box_rows, box_groups, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? LISA_OK : LISA_ECUDA;
+}
+
 namespace {
 
 int cuda_status(cudaError_t e) { return e == cudaSuccess ? LISA_OK : LISA_ECUDA; }
