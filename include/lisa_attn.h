@@ -35,7 +35,8 @@
  *       gated_out     bf16 [rows][24*256]  (the o_proj input, runner.rs:1574-1590)
  *       KV cache      bf16 [layer][4][capacity][256], K and V separately
  *                     (runner.rs:384-390, 1463-1464)
- *     q_gate and the norm weights must be 16-byte aligned (LISA_EINVAL otherwise).
+ *     q_gate and the norm weights must be 16-byte aligned, and for prefill also
+ *     k, v and gated_out (LISA_EINVAL otherwise).
  *     q_gate/k/v are f32 (LISA_DTYPE_F32, the QMV/GEMM output type of the
  *     reference) or bf16 (LISA_DTYPE_BF16). The reference rounds them to bf16
  *     before use (attention.metal:40-42), so both give identical results.

@@ -51,18 +51,17 @@ constexpr float kLog2Scale = SCALE * LOG2E;  // raw score -> exp2 argument
 constexpr uint16_t PF_PAIR = 3;  // multicast mask: both CTAs of the pair
 
 // mbarrier slots. *FULL, Q and PFULL are waited on by the pair's MMA issuer
-// (rank 0) and complete with both CTAs' loads / arrivals; *EMPTY, SFULL and
-// PVDONE are signalled to both CTAs by the MMA commits.
+// (rank 0) and complete with both CTAs' loads / arrivals; SFULL and PVDONE
+// are signalled to both CTAs by the MMA commits.
 enum {
   B_Q = 0,
-  B_KFULL = 1,    // [2]
-  B_KEMPTY = 3,   // [2]
-  B_VFULL = 5,    // [2]
-  B_VEMPTY = 7,   // [2]
-  B_SFULL = 9,    // [2] S tile in TMEM
-  B_PFULL = 11,   // [2] P tile in TMEM (8 softmax warps x 2 CTAs)
-  B_PVDONE = 13,  // [2] P.V MMA that read the P tile finished (O updated)
-  B_COUNT = 15
+  B_KFULL = 1,   // [2]
+  B_VFULL = 3,   // [2]
+  B_SFULL = 5,   // [2] S tile in TMEM; also: the K slot it read is free
+  B_PFULL = 7,   // [2] P tile in TMEM (8 softmax warps x 2 CTAs)
+  B_PVDONE = 9,  // [2] P.V finished (O updated); also: its P tile and V slot are free
+  B_G = 11,      // this CTA's gate tile in the K ring (bf16 inputs)
+  B_COUNT = 12
 };
 
 }  // namespace
@@ -155,7 +154,8 @@ __global__ void __launch_bounds__(256) prefill_prologue_kernel(const PrefillPara
 // rank 1 the next 128.
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
     prefill_attn_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                        const __grid_constant__ CUtensorMap tv, const PrefillParams p) {
+                        const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tg,
+                        const __grid_constant__ CUtensorMap to, const PrefillParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + PF_OFF_BAR);
@@ -182,6 +182,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
     tma_prefetch_desc(&tq);
     tma_prefetch_desc(&tk);
     tma_prefetch_desc(&tv);
+    tma_prefetch_desc(&to);
     for (int b = 0; b < B_COUNT; ++b) mbar_init(&bars[b], (b == B_PFULL || b == B_PFULL + 1) ? 16 : 1);
     fence_mbar_init();
   }
@@ -213,9 +214,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
 #define PT_FLUSH(role)                                                             \
   if (lane == 0)                                                                   \
     for (int k = 0; k < 8; ++k) atomicAdd(&p.trace[(role) * 8 + k], tr[k]);
+// per-tile event clocks of the first CTA (rank 0 of the heaviest pair)
+#define PE(ev, j) \
+  if (blockIdx.x == 0 && (j) < 64) p.trace[2048 + (ev) * 64 + (j)] = clock64();
 #else
 #define PT(k)
 #define PT_FLUSH(role)
+#define PE(ev, j)
 #endif
 
   if (warp == 0 && lane == 0) {
@@ -227,74 +232,115 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
     tma_load_4d_pair(smem, &tq, lead_bar(B_Q), 0, r0, 0, h);
     for (int j = 0; j < n_tiles; ++j) {
       const int s = j & 1;
-      if (j >= 2 && !mbar_wait(&bars[B_KEMPTY + s], ((j >> 1) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) break;
+      // slot s is free once S_{j-2}, which read it, has completed
+      if (j >= 2 && !mbar_wait(&bars[B_SFULL + s], ((j >> 1) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) break;
       if (rank == 0) mbar_arrive_expect_tx(&bars[B_KFULL + s], 2 * PF_KH_BYTES);
       tma_load_4d_pair(smem + PF_OFF_K + s * PF_KH_BYTES, &tk, lead_bar(B_KFULL + s), 0,
                        j * PF_BN + (int)rank * (PF_BN / 2), 0, kvh);
+    }
+    if (p.in_bf16) {
+      // once the last two S MMAs have read the K ring, it takes this CTA's
+      // gate tile: rows r0.., gate dims 256..511 of head h
+      bool free = true;
+      for (int j = max(0, n_tiles - 2); free && j < n_tiles; ++j)
+        free = mbar_wait(&bars[B_SFULL + (j & 1)], (j >> 1) & 1, p.err, ERR_TIMEOUT_EMPTY);
+      if (free) {
+        mbar_arrive_expect_tx(&bars[B_G], PF_BM * HD * 2);
+        tma_load_4d(smem + PF_OFF_K, &tg, &bars[B_G], 0, r0, 4, h);
+      }
     }
   } else if (warp == 2 && lane == 0) {
     // ---------------- V loads: this CTA's 128 dims of every V tile ----------------
     for (int j = 0; j < n_tiles; ++j) {
       const int s = j & 1;
-      if (j >= 2 && !mbar_wait(&bars[B_VEMPTY + s], ((j >> 1) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) break;
+      // slot s is free once P_{j-2}.V_{j-2}, which read it, has completed
+      if (j >= 2 && !mbar_wait(&bars[B_PVDONE + s], ((j >> 1) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) break;
       if (rank == 0) mbar_arrive_expect_tx(&bars[B_VFULL + s], 2 * PF_VH_BYTES);
       tma_load_4d_pair(smem + PF_OFF_V + s * PF_VH_BYTES, &tv, lead_bar(B_VFULL + s), 0, j * PF_BN,
                        2 * (int)rank, kvh);
     }
   } else if (warp == 1 && lane == 0 && rank == 0) {
     // ---------------- MMA issuer (rank 0 only, M = 256 over the pair) ----------------
+    // The tensor pipe keeps almost no queue: every cycle this thread spends
+    // between two MMAs is a cycle the pipe idles. So the group sequence
+    // S_0, S_1, PV_0, S_2, PV_1, ... is issued without waits between groups:
+    // the inputs of the next group are tested (non-blocking) before the last
+    // MMA of the current group, and descriptors are base + constant offsets.
     constexpr uint32_t IDESC_S = umma_idesc_bf16(2 * PF_BM, PF_BN, false);
     constexpr uint32_t IDESC_O = umma_idesc_bf16(2 * PF_BM, HD, true);
-    const uint32_t sQ = smem_u32(smem);
-    const uint32_t sK = smem_u32(smem + PF_OFF_K);
-    const uint32_t sV = smem_u32(smem + PF_OFF_V);
-    bool ok = mbar_wait(&bars[B_Q], 0, p.err, ERR_TIMEOUT_FULL);
     // S_j = Q . K_j^T: 16 k-steps of 16 dims; Q rows and K keys are stored as
-    // [64-dim group][row][64 dims]
-    auto issue_s = [&](int j) -> bool {
-      const int s = j & 1;
-      PT(7);
-      if (!mbar_wait(&bars[B_KFULL + s], (j >> 1) & 1, p.err, ERR_TIMEOUT_FULL)) return false;
-      PT(0);
-      tc_fence_after();
-      const uint32_t d = tmem + PF_TMEM_S + (uint32_t)s * PF_BN;
-#pragma unroll
-      for (int kk = 0; kk < 16; ++kk) {
-        const uint32_t g = kk >> 2, sub = kk & 3;
-        const uint64_t a = umma_desc_sw128(sQ + g * (PF_BM * 128) + sub * 32, 16, 1024);
-        const uint64_t b = umma_desc_sw128(sK + s * PF_KH_BYTES + g * ((PF_BN / 2) * 128) + sub * 32, 16, 1024);
-        umma_pair_bf16(d, a, b, IDESC_S, kk ? 1u : 0u);
-      }
-      umma_pair_commit(&bars[B_KEMPTY + s], PF_PAIR);
-      umma_pair_commit(&bars[B_SFULL + s], PF_PAIR);
-      PT(1);
-      return true;
+    // [64-dim group][row][64 dims]. O += P_j . V_j: 8 k-steps of 16 keys; P
+    // (bf16 pairs) lives over the S tile, key k at column k/2; V is stored
+    // [64-dim group][key][64 dims] and read MN-major (this CTA holds 2 of the
+    // 4 groups).
+    const uint64_t dQ = umma_desc_sw128(smem_u32(smem), 16, 1024);
+    const uint64_t dK = umma_desc_sw128(smem_u32(smem + PF_OFF_K), 16, 1024);
+    const uint64_t dV = umma_desc_sw128(smem_u32(smem + PF_OFF_V), PF_BN * 128, 1024);
+    auto s_mma = [&](int j, int kk) {
+      const uint32_t g = kk >> 2, sub = kk & 3, s = j & 1;
+      umma_pair_bf16(tmem + PF_TMEM_S + s * PF_BN, dQ + ((g * (PF_BM * 128) + sub * 32) >> 4),
+                     dK + ((s * PF_KH_BYTES + g * ((PF_BN / 2) * 128) + sub * 32) >> 4), IDESC_S, kk ? 1u : 0u);
     };
-    if (ok) ok = issue_s(0);
+    auto pv_mma = [&](int j, int kk) {
+      const uint32_t b = j & 1;
+      umma_pair_bf16_ts(tmem + PF_TMEM_O, tmem + PF_TMEM_S + b * PF_BN + kk * 8,
+                        dV + ((b * PF_VH_BYTES + kk * 2048) >> 4), IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+    };
+    auto k_ready = [&](int j) { return mbar_test_wait(&bars[B_KFULL + (j & 1)], (j >> 1) & 1); };
+    auto pv_ready = [&](int j) {
+      return mbar_test_wait(&bars[B_PFULL + (j & 1)], (j >> 1) & 1) &&
+             mbar_test_wait(&bars[B_VFULL + (j & 1)], (j >> 1) & 1);
+    };
+    bool ok = mbar_wait(&bars[B_Q], 0, p.err, ERR_TIMEOUT_FULL) &&
+              mbar_wait(&bars[B_KFULL], 0, p.err, ERR_TIMEOUT_FULL);
+    if (ok) {
+      tc_fence_after();
+#pragma unroll
+      for (int kk = 0; kk < 16; ++kk) s_mma(0, kk);
+      umma_pair_commit(&bars[B_SFULL], PF_PAIR);
+    }
+    bool next_ready = false;  // inputs of the next group already seen complete
     for (int j = 0; ok && j < n_tiles; ++j) {
       const int b = j & 1;
-      if (j + 1 < n_tiles && !issue_s(j + 1)) break;
-      PT(7);
-      if (!mbar_wait(&bars[B_PFULL + b], (j >> 1) & 1, p.err, ERR_TIMEOUT_MMA)) break;
-      PT(2);
-      if (!mbar_wait(&bars[B_VFULL + b], (j >> 1) & 1, p.err, ERR_TIMEOUT_FULL)) break;
-      PT(3);
-      tc_fence_after();
-      // O += P_j . V_j: 8 k-steps of 16 keys; P (bf16 pairs) lives over the S
-      // tile, key k at column k/2; V is stored [64-dim group][key][64 dims]
-      // and read MN-major (this CTA holds 2 of the 4 groups)
+      if (j + 1 < n_tiles) {
+        // S_{j+1}
+        if (!next_ready && !mbar_wait(&bars[B_KFULL + ((j + 1) & 1)], ((j + 1) >> 1) & 1, p.err, ERR_TIMEOUT_FULL))
+          break;
+        tc_fence_after();
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint64_t bd = umma_desc_sw128(sV + b * PF_VH_BYTES + kk * 2048, PF_BN * 128, 1024);
-        umma_pair_bf16_ts(tmem + PF_TMEM_O, tmem + PF_TMEM_S + b * PF_BN + kk * 8, bd, IDESC_O,
-                          (j > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < 15; ++kk) s_mma(j + 1, kk);
+        next_ready = pv_ready(j);
+        s_mma(j + 1, 15);
+        umma_pair_commit(&bars[B_SFULL + ((j + 1) & 1)], PF_PAIR);
+      } else {
+        next_ready = false;
       }
-      umma_pair_commit(&bars[B_VEMPTY + b], PF_PAIR);
+      // P_j . V_j
+      if (!next_ready && !(mbar_wait(&bars[B_PFULL + b], (j >> 1) & 1, p.err, ERR_TIMEOUT_MMA) &&
+                           mbar_wait(&bars[B_VFULL + b], (j >> 1) & 1, p.err, ERR_TIMEOUT_FULL)))
+        break;
+      tc_fence_after();
+#pragma unroll
+      for (int kk = 0; kk < 7; ++kk) pv_mma(j, kk);
+      next_ready = j + 2 < n_tiles && k_ready(j + 2);
+      pv_mma(j, 7);
       umma_pair_commit(&bars[B_PVDONE + b], PF_PAIR);
-      PT(4);
     }
     PT_FLUSH(0);
   }
+#if defined(LISA_PREFILL_TRACE) || defined(LISA_PREFILL_OBSERVE)
+  else if (warp == 3 && lane == 0 && blockIdx.x == 0) {
+    // observer: completion clocks of S_j (event 8) and P_j.V_j (event 9)
+    for (int j = 0; j < n_tiles && j < 64; ++j) {
+      mbar_wait(&bars[B_SFULL + (j & 1)], (j >> 1) & 1, nullptr, 0);
+      p.trace[2048 + 8 * 64 + j] = clock64();
+      if (j >= 1) {
+        mbar_wait(&bars[B_PVDONE + ((j - 1) & 1)], ((j - 1) >> 1) & 1, nullptr, 0);
+        p.trace[2048 + 9 * 64 + j - 1] = clock64();
+      }
+    }
+  }
+#endif
   else if (warp >= 4) {
     // ---------------- softmax / correction / epilogue (warps 4..11) ----------------
     // Warp 4+w and warp 8+w share TMEM lanes 32w..32w+31 (one query row per
@@ -315,6 +361,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
         break;
       }
       PT(0);
+      if (lane == 0 && warp == 4) { PE(4, j); }
+      if (lane == 0 && j == 10) { PE(14, warp - 4); }
       tc_fence_after();
       uint32_t sa[32], sb[32];
       const uint32_t scol = PF_TMEM_S + b * PF_BN + half * 64;
@@ -392,59 +440,85 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster_relaxed(lead_bar(B_PFULL + b));
+      if (lane == 0 && warp == 4) { PE(5, j); }
+      if (lane == 0 && warp == 8) { PE(6, j); }
+      if (lane == 0 && j == 10) { PE(13, warp - 4); }
       PT(4);
     }
 #ifdef LISA_PREFILL_TRACE
     if (threadIdx.x == 128) p.trace[64 + blockIdx.x * 8 + 3] = global_timer_ns();
 #endif
-    // gate values of this row and half, prefetched while the last P.V runs
+    // Gate values of this row and half. bf16 inputs: the K producer has
+    // brought this CTA's gate tile into the K ring ([group][row][64],
+    // 128-byte swizzle) once the last S was computed. f32 inputs: loaded
+    // here, rounded to bf16 as the reference does.
     const int r = r0 + row;
     uint32_t gpk[64];
-    if (ok && r < p.rows) {
+    if (!p.in_bf16 && ok && r < p.rows) {
       const size_t gbase = (size_t)r * QROW + (size_t)h * 512 + 256 + half * 128;
 #pragma unroll
       for (int g8 = 0; g8 < 16; ++g8) {
         float gv[8];
-        load8_in(p.q_gate, gbase + g8 * 8, p.in_bf16, gv);
+        load8_in(p.q_gate, gbase + g8 * 8, 0, gv);
 #pragma unroll
         for (int i = 0; i < 4; ++i) gpk[g8 * 4 + i] = pack_bf16x2(gv[2 * i], gv[2 * i + 1]);
       }
     }
     const int last = n_tiles - 1;
     ok = ok && mbar_wait(&bars[B_PVDONE + (last & 1)], (last >> 1) & 1, p.err, ERR_TIMEOUT_MMA);
+#ifdef LISA_PREFILL_TRACE
+    if (threadIdx.x == 128) p.trace[64 + blockIdx.x * 8 + 2] = global_timer_ns();
+#endif
     // Sum the two halves' denominators (half 0 + half 1).
     xsum[half * PF_BM + row] = l;
     named_bar_sync(2 + wi, 64);
     const float l_row = xsum[row] + xsum[PF_BM + row];
+    if (p.in_bf16) ok = ok && mbar_wait(&bars[B_G], 0, p.err, ERR_TIMEOUT_FULL);
+    // gated rows staged in the (now idle) V ring as [group][row][64] with the
+    // 128-byte swizzle, then written by one TMA store (rows >= p.rows clipped)
+    uint8_t* stage = smem + PF_OFF_V;
+    const uint8_t* gtile = smem + PF_OFF_K;
     if (ok) {
       tc_fence_after();
       const float inv_l = 1.0f / l_row;
 #pragma unroll
       for (int c = 0; c < HD / 64; ++c) {
-        const int col = half * (HD / 2) + c * 32;
+        const int col = half * (HD / 2) + c * 32;  // first of this pass's 32 dims
+        const int grp = col >> 6, ch0 = (col & 63) >> 3;
         uint32_t ov[32];
         tmem_ld32(lane_addr + PF_TMEM_O + col, ov);
-        tmem_wait_ld();
-        if (r < p.rows) {
-          uint32_t outw[16];
+        uint32_t gw[16];
+        if (p.in_bf16) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const uint32_t gg = gpk[c * 16 + i];
-            float y[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const float gv = bf16_bits_to_f32(e ? gg >> 16 : gg & 0xffffu);
-              const float sg = fast_rcp(1.0f + fast_exp2(-LOG2E * gv));
-              y[e] = __uint_as_float(ov[2 * i + e]) * inv_l * sg;
-            }
-            outw[i] = pack_bf16x2(y[0], y[1]);
+          for (int i = 0; i < 4; ++i) {
+            const uint4 g4 = *reinterpret_cast<const uint4*>(gtile + grp * (PF_BM * 128) + row * 128 +
+                                                             (((ch0 + i) ^ (row & 7)) << 4));
+            gw[4 * i] = g4.x; gw[4 * i + 1] = g4.y; gw[4 * i + 2] = g4.z; gw[4 * i + 3] = g4.w;
           }
-          uint4* dst = reinterpret_cast<uint4*>(p.gated_out + (size_t)r * OROW + h * HD + col);
+        } else {
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            dst[i] = make_uint4(outw[4 * i], outw[4 * i + 1], outw[4 * i + 2], outw[4 * i + 3]);
+          for (int i = 0; i < 16; ++i) gw[i] = gpk[c * 16 + i];
         }
+        tmem_wait_ld();
+        uint32_t outw[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float2 g2 = unpack_bf16x2(gw[i]);
+          outw[i] = pack_bf16x2(__uint_as_float(ov[2 * i]) * inv_l * fast_sigmoid(g2.x),
+                                __uint_as_float(ov[2 * i + 1]) * inv_l * fast_sigmoid(g2.y));
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          *reinterpret_cast<uint4*>(stage + grp * (PF_BM * 128) + row * 128 + (((ch0 + i) ^ (row & 7)) << 4)) =
+              make_uint4(outw[4 * i], outw[4 * i + 1], outw[4 * i + 2], outw[4 * i + 3]);
       }
+    }
+    fence_proxy_async_smem();
+    named_bar_sync(6, 256);  // the staged tile is complete
+    if (ok && threadIdx.x == 128) {
+      tma_store_4d(&to, stage, 0, r0, 0, h);
+      bulk_commit_group();
+      bulk_wait_read();  // the staging must stay until the store has read it
     }
     PT(5);
     if (warp == 4) { PT_FLUSH(1); }
@@ -486,18 +560,20 @@ cudaError_t launch_prefill(const PrefillParams& p_in, int num_sms, cudaStream_t 
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk, tv, tg = {}, to;
   const uint32_t kv_rows = p.base + (uint32_t)p.rows;
   if (lisa_encode_group_map(&tq, p.q_ws, PF_MAX_ROWS, PF_MAX_ROWS, QH, PF_BM, 4) != 0 ||
       lisa_encode_group_map(&tk, p.k_cache, kv_rows, p.capacity, KVH, PF_BN / 2, 4) != 0 ||
-      lisa_encode_group_map(&tv, p.v_cache, kv_rows, p.capacity, KVH, PF_BN, 2) != 0)
+      lisa_encode_group_map(&tv, p.v_cache, kv_rows, p.capacity, KVH, PF_BN, 2) != 0 ||
+      lisa_encode_rows_map(&to, p.gated_out, (uint32_t)p.rows, OROW, 4, QH, HD, PF_BM) != 0 ||
+      (p.in_bf16 && lisa_encode_rows_map(&tg, p.q_gate, (uint32_t)p.rows, QROW, 8, QH, 512, PF_BM) != 0))
     return cudaErrorInvalidValue;
   const int n_qt = (p.rows + PF_BM - 1) / PF_BM;
   const int n_pairs = (n_qt + 1) / 2;
   cfg.gridDim = dim3(n_pairs * QH * 2);
   cfg.blockDim = dim3(PF_THREADS);
   cfg.dynamicSmemBytes = PF_SMEM_BYTES;
-  return cudaLaunchKernelEx(&cfg, prefill_attn_kernel, tq, tk, tv, p);
+  return cudaLaunchKernelEx(&cfg, prefill_attn_kernel, tq, tk, tv, tg, to, p);
 }
 
 }  // namespace lisa

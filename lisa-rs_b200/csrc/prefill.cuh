@@ -13,6 +13,11 @@ int lisa_encode_kv_map(CUtensorMap* map, const void* base, uint32_t rows, uint32
 // {64, box_rows, box_groups, 1} landing as [group][row][64]. Defined in runtime.cu.
 int lisa_encode_group_map(CUtensorMap* map, const void* base, uint32_t rows, uint32_t window_rows, uint32_t planes,
                           uint32_t box_rows, uint32_t box_groups);
+// A bf16 [rows][heads][head_elems] array (row stride row_elems) as 64-element
+// groups: dims {64, rows, groups, heads}, boxes {64, box_rows, 4, 1}. Defined
+// in runtime.cu.
+int lisa_encode_rows_map(CUtensorMap* map, const void* base, uint32_t rows, uint32_t row_elems, uint32_t groups,
+                         uint32_t heads, uint32_t head_elems, uint32_t box_rows);
 
 namespace lisa {
 
@@ -35,7 +40,7 @@ struct PrefillParams {
   uint16_t* gated_out;  // [rows][6144]
   int* err;
   float inv_freq[32];  // filled by launch_prefill
-#ifdef LISA_PREFILL_TRACE
+#if defined(LISA_PREFILL_TRACE) || defined(LISA_PREFILL_OBSERVE)
   unsigned long long* trace;  // debug builds only
 #endif
 };

@@ -97,6 +97,25 @@ int lisa_encode_group_map(CUtensorMap* map, const void* base, uint32_t rows, uin
   return r == CUDA_SUCCESS ? LISA_OK : LISA_ECUDA;
 }
 
+// Tensor map over a bf16 [rows][heads][head_elems] array (row stride
+// row_elems) seen as 64-element groups: dims {64, rows, groups, heads} with
+// strides {row_elems * 2, 128, head_elems * 2} bytes; boxes {64, box_rows, 4,
+// 1} (one head, four groups) with 128-byte swizzle, [group][row][64] in
+// shared memory. Rows >= `rows` read as zero and are not written.
+int lisa_encode_rows_map(CUtensorMap* map, const void* base, uint32_t rows, uint32_t row_elems, uint32_t groups,
+                         uint32_t heads, uint32_t head_elems, uint32_t box_rows) {
+  auto enc = get_encode();
+  if (!enc) return LISA_ECUDA;
+  cuuint64_t dims[4] = {64, rows, groups, heads};
+  cuuint64_t strides[3] = {(cuuint64_t)row_elems * 2, 128, (cuuint64_t)head_elems * 2};
+  cuuint32_t box[4] = {64, box_rows, 4, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? LISA_OK : LISA_ECUDA;
+}
+
 namespace {
 
 int cuda_status(cudaError_t e) { return e == cudaSuccess ? LISA_OK : LISA_ECUDA; }
@@ -244,6 +263,8 @@ int lisa_attn_prefill_chunk(lisa_attn_ctx* c, int layer, uint32_t base, int rows
   int s = check_layer_args(c, layer, in_dtype, q_gate, k, v, qn, kn, gated_out);
   if (s != LISA_OK) return s;
   if (rows < 1 || rows > PF_MAX_ROWS) return LISA_EINVAL;
+  // vector loads of the inputs and TMA on q_gate / gated_out: 16-byte alignment
+  if (((uintptr_t)q_gate | (uintptr_t)k | (uintptr_t)v | (uintptr_t)gated_out) & 15) return LISA_EINVAL;
   if ((uint64_t)base + rows > c->capacity) return LISA_ENOSPC;
   DeviceGuard guard(c->device);
   const size_t off = (size_t)layer * layer_elems(c);
