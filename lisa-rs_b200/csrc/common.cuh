@@ -117,6 +117,30 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
       : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
   return make_float2(__uint_as_float((uint32_t)d), __uint_as_float((uint32_t)(d >> 32)));
 }
+// 2^x for a pair of arguments on the FMA pipe (no SFU): x = n + f with n the
+// nearest integer (f in [-1/2, 1/2]), 2^f by a degree-4 polynomial fitted
+// here to relative error 2.7e-6 (weighted least squares on Chebyshev nodes),
+// and n added to the exponent field. Arguments are clamped at -125 so that the
+// result stays a normal number (2^f >= 2^-1/2 has biased exponent >= 126):
+// -inf gives 2^-125, not 0, which no bf16 sum or product can tell apart.
+// Arguments must be below 128.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23: x + kRound rounds x to an integer
+  x.x = fmaxf(x.x, -125.0f);
+  x.y = fmaxf(x.y, -125.0f);
+  const float2 t = fadd2(x, make_float2(kRound, kRound));
+  const float2 n = fadd2(t, make_float2(-kRound, -kRound));
+  const float2 f = ffma2(n, make_float2(-1.0f, -1.0f), x);
+  float2 p = ffma2(make_float2(0.009570094756782055f, 0.009570094756782055f), f,
+                   make_float2(0.05591785907745361f, 0.05591785907745361f));
+  p = ffma2(p, f, make_float2(0.240247443318367f, 0.240247443318367f));
+  p = ffma2(p, f, make_float2(0.6931217908859253f, 0.6931217908859253f));
+  p = ffma2(p, f, make_float2(0.9999992847442627f, 0.9999992847442627f));
+  // the low bits of t hold n (two's complement); shifted into the exponent
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
+}
+
 // The two bf16 halves of a packed word as f32 (exact).
 __device__ __forceinline__ float2 unpack_bf16x2(uint32_t w) {
   return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));

@@ -397,8 +397,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
         mr = mnew;
       }
       // P = exp2(x * scale*log2e - m), rounded to bf16 and written over the S
-      // tile 16 keys at a time so the TMEM stores overlap the exponentials;
-      // the denominator sums the rounded values the P.V MMA uses.
+      // tile 16 keys at a time so the TMEM stores overlap the exponentials.
+      // 3 of every 8 key pairs are exponentiated on the FMA pipe, the rest on
+      // the SFU, which alone would bound this loop. The denominator sums the
+      // f32 values, as the reference's f32 softmax does.
       const float2 cc = make_float2(kLog2Scale, kLog2Scale);
       const float2 nm = make_float2(-mr * kLog2Scale, -mr * kLog2Scale);
       float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
@@ -408,9 +410,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           const float2 e = ffma2(make_float2(x[16 * q + 2 * c], x[16 * q + 2 * c + 1]), cc, nm);
-          pk[c] = pack_bf16x2(fast_exp2(e.x), fast_exp2(e.y));
-          if (c & 1) acc1 = fadd2(acc1, unpack_bf16x2(pk[c]));
-          else acc0 = fadd2(acc0, unpack_bf16x2(pk[c]));
+          const float2 pe = c < 3 ? exp2_poly2(e) : make_float2(fast_exp2(e.x), fast_exp2(e.y));
+          pk[c] = pack_bf16x2(pe.x, pe.y);
+          if (c & 1) acc1 = fadd2(acc1, pe);
+          else acc0 = fadd2(acc0, pe);
         }
         tmem_st8(lane_addr + PF_TMEM_S + b * PF_BN + half * 32 + q * 8, pk);
       }
