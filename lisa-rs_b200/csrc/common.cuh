@@ -65,6 +65,10 @@ __device__ __forceinline__ float load_in_bf16(const void* p, size_t i, int is_bf
 // rounded to f32 (host_rope_table computes the same values on the host).
 __device__ __forceinline__ void rope_cs(uint32_t pos, float inv_freq, float& c, float& s) {
   const float angle = (float)pos * inv_freq;
+#ifdef DIAG_F32_SINCOS
+  sincosf(angle, &s, &c);
+  return;
+#endif
   double sd, cd;
   sincos((double)angle, &sd, &cd);
   c = (float)cd;

@@ -84,20 +84,43 @@ __device__ __forceinline__ void load8_in(const void* src, size_t idx, int is_bf1
   }
 }
 
+// Eight consecutive inputs as packed bf16 pairs (f32 inputs rounded to
+// nearest-even, as the reference rounds its inputs), idx a multiple of 8.
+__device__ __forceinline__ uint4 load8_bf16(const void* src, size_t idx, int is_bf16) {
+  if (is_bf16) return *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(src) + idx);
+  const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(src) + idx);
+  const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(src) + idx + 4);
+  return make_uint4(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w), pack_bf16x2(b.x, b.y), pack_bf16x2(b.z, b.w));
+}
+
 // One 256-thread CTA per prompt row; warp w handles items w, w+8, w+16, w+24
-// (items 0..23 are the query heads, 24..27 the KV heads). The row's 32 RoPE
-// (cos, sin) pairs are computed once into shared memory while the loads are in
-// flight. Lane l holds dims 8l..8l+7; the RoPE partner of dims 0..31
-// (lanes 0..3) is dims 32..63 (lanes 4..7).
-__global__ void __launch_bounds__(256) prefill_prologue_kernel(const PrefillParams p) {
-  __shared__ float s_cos[ROT_PAIRS], s_sin[ROT_PAIRS];
+// (items 0..23 are the query heads, 24..27 the KV heads). Lane l holds dims
+// 8l..8l+7; the RoPE partner of dims 0..31 (lanes 0..3) is dims 32..63
+// (lanes 4..7). Warp 0 first computes the row's 32 RoPE (cos, sin) pairs (one
+// double-precision sincos per lane) into shared memory, then every warp issues
+// its loads; the one CTA barrier falls inside the load latency. At most 64
+// registers: all 512 CTAs of a chunk fit in one wave.
+__global__ void __launch_bounds__(256, 4) prefill_prologue_kernel(const PrefillParams p) {
+  __shared__ float s_cs[2 * ROT_PAIRS];  // pair j: cos at [2j], sin at [2j + 1]
   pdl_wait_primary();       // the previous chunk may still read q_ws
   pdl_launch_dependents();  // let the attention kernel set up meanwhile
   const int r = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t pos = p.base + r;
+#ifdef LISA_PREFILL_TRACE
+  if (threadIdx.x == 0) atomicMin(&p.trace[32], (unsigned long long)global_timer_ns());
+  if (threadIdx.x == 0 && r < 512) p.trace[3072 + r] = global_timer_ns();
+#endif
+  if (warp == 0) {
+    float c, sn;
+    rope_cs(pos, p.inv_freq[lane], c, sn);
+    s_cs[2 * lane] = c;
+    s_cs[2 * lane + 1] = sn;
+  }
   constexpr int NI = 4;  // items per warp
-  float x[NI][8], v[NI][8];  // v: the V row of KV items
+  uint4 xr[NI], vr = make_uint4(0, 0, 0, 0);  // 8 inputs as bf16 pairs; vr: the V row of the KV item
+  const uint4 qw4 = *reinterpret_cast<const uint4*>(p.q_norm_w + lane * 8);
+  const uint4 kw4 = *reinterpret_cast<const uint4*>(p.k_norm_w + lane * 8);
 #pragma unroll
   for (int t = 0; t < NI; ++t) {
     const int hh = warp + 8 * t;
@@ -105,48 +128,62 @@ __global__ void __launch_bounds__(256) prefill_prologue_kernel(const PrefillPara
     const bool is_q = hh < QH;
     const size_t in = is_q ? (size_t)r * QROW + (size_t)hh * 512 + lane * 8
                            : (size_t)r * KROW + (size_t)(hh - QH) * HD + lane * 8;
-    load8_in(is_q ? p.q_gate : p.k_in, in, p.in_bf16, x[t]);
-    if (!is_q) load8_in(p.v_in, in, p.in_bf16, v[t]);
+    xr[t] = load8_bf16(is_q ? p.q_gate : p.k_in, in, p.in_bf16);
+    if (!is_q) vr = load8_bf16(p.v_in, in, p.in_bf16);
   }
-  if (threadIdx.x < ROT_PAIRS) rope_cs(pos, p.inv_freq[threadIdx.x], s_cos[threadIdx.x], s_sin[threadIdx.x]);
   __syncthreads();  // RoPE table ready
+  // lanes 0..7 rotate: the first half by -sin, the second by +sin; other
+  // lanes multiply by (1, 0)
+  const float rot_c = lane < 8 ? 1.0f : 0.0f;
+  const float rot_s = lane < 4 ? -1.0f : rot_c;
 #pragma unroll
   for (int t = 0; t < NI; ++t) {
     const int hh = warp + 8 * t;
     if (hh >= QH + KVH) continue;  // uniform per warp
     const bool is_q = hh < QH;
-    const uint16_t* w = is_q ? p.q_norm_w : p.k_norm_w;
+    const uint4 w4 = is_q ? qw4 : kw4;
+    const uint32_t wv[4] = {w4.x, w4.y, w4.z, w4.w};
+    const uint32_t xw[4] = {xr[t].x, xr[t].y, xr[t].z, xr[t].w};
+    float x8[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = unpack_bf16x2(xw[i]);
+      x8[2 * i] = f.x;
+      x8[2 * i + 1] = f.y;
+    }
     float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) ss += x[t][i] * x[t][i];
+    for (int i = 0; i < 8; ++i) ss = fmaf(x8[i], x8[i], ss);
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
     const float inv = 1.0f / sqrtf(ss / 256.0f + p.eps);
+    float n[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) n[i] = x8[i] * inv * bf16_bits_to_f32((wv[i >> 1] >> ((i & 1) * 16)) & 0xffffu);
     float o[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float n = x[t][i] * inv * bf16_bits_to_f32(w[lane * 8 + i]);
-      const float partner = __shfl_xor_sync(0xffffffffu, n, 4);
-      o[i] = n;
-      if (lane < 8) {
-        const int j = (lane & 3) * 8 + i;
-        o[i] = lane < 4 ? n * s_cos[j] - partner * s_sin[j] : n * s_cos[j] + partner * s_sin[j];
-      }
+      const float partner = __shfl_xor_sync(0xffffffffu, n[i], 4);
+      const float2 cs = *reinterpret_cast<const float2*>(&s_cs[2 * ((lane & 3) * 8 + i)]);
+      const float c = fmaf(cs.x, rot_c, 1.0f - rot_c);  // cos, or 1 on lanes >= 8
+      o[i] = fmaf(partner, cs.y * rot_s, n[i] * c);     // lanes >= 8: n[i] * 1 + partner * 0
     }
     const uint4 packed = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
                                     pack_bf16x2(o[6], o[7]));
     if (is_q) {
-      // chunk-major [head][chunk = lane][row]: a warp reading 32 rows of one
-      // chunk touches 512 contiguous bytes
+      // q_ws [head][row][256]
       *reinterpret_cast<uint4*>(p.q_ws + ((size_t)hh * PF_MAX_ROWS + r) * HD + lane * 8) = packed;
     } else {
       const size_t out = ((size_t)(hh - QH) * p.capacity + pos) * HD + lane * 8;
       *reinterpret_cast<uint4*>(p.k_cache + out) = packed;
-      *reinterpret_cast<uint4*>(p.v_cache + out) =
-          make_uint4(pack_bf16x2(v[t][0], v[t][1]), pack_bf16x2(v[t][2], v[t][3]), pack_bf16x2(v[t][4], v[t][5]),
-                     pack_bf16x2(v[t][6], v[t][7]));
+      *reinterpret_cast<uint4*>(p.v_cache + out) = vr;
     }
   }
+#ifdef LISA_PREFILL_TRACE
+  __syncthreads();
+  if (threadIdx.x == 0) atomicMax(&p.trace[33], (unsigned long long)global_timer_ns());
+  if (threadIdx.x == 0 && r < 512) p.trace[3584 + r] = global_timer_ns();
+#endif
 }
 
 // Grid: clusters of 2 CTAs, n_pairs * 24 clusters, heaviest (last) query
