@@ -40,18 +40,17 @@ __device__ __forceinline__ uint32_t chunk_tiles(uint32_t chunk, uint32_t extent)
   return (n + DEC_TILE - 1) / DEC_TILE;
 }
 
-// Issues the TMA loads of one 64-token stage: K and V, 4 boxes of 64 dims
-// (128-byte swizzled rows) each.
+// Issues the TMA loads of one 64-token stage: K and V, one box each of all
+// four 64-dim groups (32 KB, landing as [group][token][64 dims] with
+// 128-byte swizzled rows). A TMA operation costs a fixed latency whatever its
+// size, so two large boxes stream faster than eight small ones.
 // The KV stream is read once: it is loaded with an evict-first L2 policy so
 // it does not push the chunk partials (read back by the combine) out of L2.
 __device__ __forceinline__ void issue_tile(uint8_t* stage, uint64_t* full, const CUtensorMap* tk,
                                            const CUtensorMap* tv, uint32_t row0, int kvh, uint64_t pol) {
   mbar_arrive_expect_tx(full, DEC_STAGE_BYTES);
-#pragma unroll
-  for (int st = 0; st < 4; ++st) {
-    tma_load_3d_hint(stage + st * (DEC_TILE * 128), tk, full, st * 64, (int)row0, kvh, pol);
-    tma_load_3d_hint(stage + DEC_STAGE_BYTES / 2 + st * (DEC_TILE * 128), tv, full, st * 64, (int)row0, kvh, pol);
-  }
+  tma_load_4d_hint(stage, tk, full, 0, (int)row0, 0, kvh, pol);
+  tma_load_4d_hint(stage + DEC_STAGE_BYTES / 2, tv, full, 0, (int)row0, 0, kvh, pol);
 }
 
 // Normalises + ropes one new K row (position pos) and rounds one V row, 8 dims

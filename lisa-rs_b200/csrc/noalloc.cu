@@ -104,8 +104,8 @@ extern "C" int lisa_attn_decode_noalloc(void* k_cache, void* v_cache, uint32_t c
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(p.err, 0, 128, st) != cudaSuccess) return LISA_ECUDA;
   CUtensorMap tk, tv;
-  if (lisa_encode_kv_map(&tk, k_cache, p.extent, capacity, DEC_TILE, KVH) != LISA_OK ||
-      lisa_encode_kv_map(&tv, v_cache, p.extent, capacity, DEC_TILE, KVH) != LISA_OK)
+  if (lisa_encode_group_map(&tk, k_cache, p.extent, capacity, KVH, DEC_TILE, 4) != LISA_OK ||
+      lisa_encode_group_map(&tv, v_cache, p.extent, capacity, KVH, DEC_TILE, 4) != LISA_OK)
     return LISA_ECUDA;
   return launch_decode(p, rows, tk, tv, sms, st) == cudaSuccess ? LISA_OK : LISA_ECUDA;
 }

@@ -5,11 +5,7 @@
 #include <stdint.h>
 
 // Encodes a TMA map over a bf16 [planes][window_rows][256] array (a cache
-// window has 4 planes): dims {256, rows, planes}, boxes {64, box_rows, 1},
-// SWIZZLE_128B. Defined in runtime.cu.
-int lisa_encode_kv_map(CUtensorMap* map, const void* base, uint32_t rows, uint32_t window_rows, uint32_t box_rows,
-                       uint32_t planes);
-// The same array seen as 64-dim groups: dims {64, rows, 4, planes}, boxes
+// window has 4 planes) seen as 64-dim groups: dims {64, rows, 4, planes}, boxes
 // {64, box_rows, box_groups, 1} landing as [group][row][64]. Defined in runtime.cu.
 int lisa_encode_group_map(CUtensorMap* map, const void* base, uint32_t rows, uint32_t window_rows, uint32_t planes,
                           uint32_t box_rows, uint32_t box_groups);

@@ -61,23 +61,6 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
 
 }  // namespace
 
-// Tensor map over one layer's cache window: dims {256, rows, 4 heads}, row
-// stride 512 B, head stride window_rows * 512 B; boxes {64, box_rows, 1} with
-// 128-byte swizzle; positions >= rows read as zero.
-int lisa_encode_kv_map(CUtensorMap* map, const void* base, uint32_t rows, uint32_t window_rows, uint32_t box_rows,
-                       uint32_t planes) {
-  auto enc = get_encode();
-  if (!enc) return LISA_ECUDA;
-  cuuint64_t dims[3] = {256, rows, planes};
-  cuuint64_t strides[2] = {512, (cuuint64_t)window_rows * 512};
-  cuuint32_t box[3] = {64, box_rows, 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? LISA_OK : LISA_ECUDA;
-}
-
 // Tensor map over a bf16 [planes][window_rows][256] array seen as 64-dim
 // groups: dims {64, rows, 4 groups, planes} (strides 512 B, 128 B,
 // window_rows * 512 B); boxes {64, box_rows, box_groups, 1} with 128-byte
@@ -170,8 +153,8 @@ int run_decode(uint16_t* kc, uint16_t* vc, uint32_t window_rows, uint32_t kv_lo,
   // the kernel bulk-copies q rows and the q gains: 16-byte alignment required
   if (((uintptr_t)q_gate & 15) || ((uintptr_t)qn & 15)) return LISA_EINVAL;
   CUtensorMap tk, tv;
-  int s = lisa_encode_kv_map(&tk, kc, p.extent, window_rows, DEC_TILE, KVH);
-  if (s == LISA_OK) s = lisa_encode_kv_map(&tv, vc, p.extent, window_rows, DEC_TILE, KVH);
+  int s = lisa_encode_group_map(&tk, kc, p.extent, window_rows, KVH, DEC_TILE, 4);
+  if (s == LISA_OK) s = lisa_encode_group_map(&tv, vc, p.extent, window_rows, KVH, DEC_TILE, 4);
   if (s != LISA_OK) return s;
   return cuda_status(launch_decode(p, rows, tk, tv, num_sms, stream));
 }
