@@ -188,7 +188,7 @@ int lisa_attn_merge_windows(int n_parts, int rows, const float* part_o, const fl
  * decode path. Same work and results as lisa_attn_decode, but over a KV cache
  * the caller owns (k_cache / v_cache, [4][capacity][256] bf16, row i =
  * position i) and with its scratch in a fixed array compiled into the library
- * (about 12.6 MB per GPU that loads it, held until the process exits), so the
+ * (about 3.7 MB per GPU that loads it, held until the process exits), so the
  * call allocates nothing.
  *   - base + rows must not exceed LISA_ATTN_NOALLOC_MAX_POSITIONS; larger
  *     requests return LISA_E2BIG (use lisa_attn_decode for them).
