@@ -156,7 +156,7 @@ __global__ void __launch_bounds__(256, 4) prefill_prologue_kernel(const PrefillP
     for (int i = 0; i < 8; ++i) ss = fmaf(x8[i], x8[i], ss);
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-    const float inv = 1.0f / sqrtf(ss / 256.0f + p.eps);
+    const float inv = rsqrtf(ss / 256.0f + p.eps);  // the shader's rsqrt (attention.metal:364-401)
     float n[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) n[i] = x8[i] * inv * bf16_bits_to_f32((wv[i >> 1] >> ((i & 1) * 16)) & 0xffffu);
@@ -235,8 +235,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
   const uint32_t lead_bars = cluster_map(smem_u32(bars), 0);
   auto lead_bar = [&](int i) -> uint32_t { return lead_bars + 8u * (uint32_t)i; };
   // Setup above overlaps the prologue kernel; its q_ws / KV writes are read
-  // only after it has completed.
-  pdl_wait_primary();
+  // only after it has completed. The K/V producers first issue the loads of
+  // the first two key tiles when they hold only positions below `base`
+  // (written by earlier calls), then wait too.
+  const int n_early = min(min(2, n_tiles), (int)(p.base / PF_BN));
+  if (!((warp == 0 || warp == 2) && lane == 0)) pdl_wait_primary();
   pdl_launch_dependents();
 #ifdef LISA_PREFILL_TRACE
   if (threadIdx.x == 0) p.trace[64 + blockIdx.x * 8 + 1] = global_timer_ns();
@@ -265,15 +268,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
     // Each CTA loads its own 128 query rows and its half (64 keys) of every
     // K tile; completion is counted on rank 0's barriers, whose expected
     // byte count rank 0 sets for both.
-    if (rank == 0) mbar_arrive_expect_tx(&bars[B_Q], 2 * PF_Q_BYTES);
-    tma_load_4d_pair(smem, &tq, lead_bar(B_Q), 0, r0, 0, h);
-    for (int j = 0; j < n_tiles; ++j) {
+    auto load_k = [&](int j) {
       const int s = j & 1;
-      // slot s is free once S_{j-2}, which read it, has completed
-      if (j >= 2 && !mbar_wait(&bars[B_SFULL + s], ((j >> 1) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) break;
       if (rank == 0) mbar_arrive_expect_tx(&bars[B_KFULL + s], 2 * PF_KH_BYTES);
       tma_load_4d_pair(smem + PF_OFF_K + s * PF_KH_BYTES, &tk, lead_bar(B_KFULL + s), 0,
                        j * PF_BN + (int)rank * (PF_BN / 2), 0, kvh);
+    };
+    for (int j = 0; j < n_early; ++j) load_k(j);
+    pdl_wait_primary();
+    if (rank == 0) mbar_arrive_expect_tx(&bars[B_Q], 2 * PF_Q_BYTES);
+    tma_load_4d_pair(smem, &tq, lead_bar(B_Q), 0, r0, 0, h);
+    for (int j = n_early; j < n_tiles; ++j) {
+      // slot j & 1 is free once S_{j-2}, which read it, has completed
+      if (j >= 2 && !mbar_wait(&bars[B_SFULL + (j & 1)], ((j >> 1) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) break;
+      load_k(j);
     }
     if (p.in_bf16) {
       // once the last two S MMAs have read the K ring, it takes this CTA's
@@ -288,13 +296,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
     }
   } else if (warp == 2 && lane == 0) {
     // ---------------- V loads: this CTA's 128 dims of every V tile ----------------
-    for (int j = 0; j < n_tiles; ++j) {
+    auto load_v = [&](int j) {
       const int s = j & 1;
-      // slot s is free once P_{j-2}.V_{j-2}, which read it, has completed
-      if (j >= 2 && !mbar_wait(&bars[B_PVDONE + s], ((j >> 1) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) break;
       if (rank == 0) mbar_arrive_expect_tx(&bars[B_VFULL + s], 2 * PF_VH_BYTES);
       tma_load_4d_pair(smem + PF_OFF_V + s * PF_VH_BYTES, &tv, lead_bar(B_VFULL + s), 0, j * PF_BN,
                        2 * (int)rank, kvh);
+    };
+    for (int j = 0; j < n_early; ++j) load_v(j);
+    pdl_wait_primary();
+    for (int j = n_early; j < n_tiles; ++j) {
+      // slot j & 1 is free once P_{j-2}.V_{j-2}, which read it, has completed
+      if (j >= 2 && !mbar_wait(&bars[B_PVDONE + (j & 1)], ((j >> 1) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) break;
+      load_v(j);
     }
   } else if (warp == 1 && lane == 0 && rank == 0) {
     // ---------------- MMA issuer (rank 0 only, M = 256 over the pair) ----------------
