@@ -132,22 +132,28 @@ __global__ void __launch_bounds__(256, 4) prefill_prologue_kernel(const PrefillP
     if (!is_q) vr = load8_bf16(p.v_in, in, p.in_bf16);
   }
   __syncthreads();  // RoPE table ready
-  // lanes 0..7 rotate: the first half by -sin, the second by +sin; other
-  // lanes multiply by (1, 0)
-  const float rot_c = lane < 8 ? 1.0f : 0.0f;
-  const float rot_s = lane < 4 ? -1.0f : rot_c;
+  // Per-lane factors shared by every item of the row (the same position):
+  // element i of lane l becomes n_i * rc_i + partner_i * rs_i, with (rc, rs)
+  // = (cos, -sin) on lanes 0..3, (cos, +sin) on lanes 4..7 and (1, 0) on the
+  // other lanes; and the query gains as f32.
+  float rc[8], rs[8], gq[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float2 cs = *reinterpret_cast<const float2*>(&s_cs[2 * ((lane & 3) * 8 + i)]);
+    rc[i] = lane < 8 ? cs.x : 1.0f;
+    rs[i] = lane < 4 ? -cs.y : lane < 8 ? cs.y : 0.0f;
+    const float2 g2 = unpack_bf16x2((&qw4.x)[i >> 1]);
+    gq[i] = (i & 1) ? g2.y : g2.x;
+  }
 #pragma unroll
   for (int t = 0; t < NI; ++t) {
     const int hh = warp + 8 * t;
     if (hh >= QH + KVH) continue;  // uniform per warp
     const bool is_q = hh < QH;
-    const uint4 w4 = is_q ? qw4 : kw4;
-    const uint32_t wv[4] = {w4.x, w4.y, w4.z, w4.w};
-    const uint32_t xw[4] = {xr[t].x, xr[t].y, xr[t].z, xr[t].w};
     float x8[8];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const float2 f = unpack_bf16x2(xw[i]);
+      const float2 f = unpack_bf16x2((&xr[t].x)[i]);
       x8[2 * i] = f.x;
       x8[2 * i + 1] = f.y;
     }
@@ -159,14 +165,19 @@ __global__ void __launch_bounds__(256, 4) prefill_prologue_kernel(const PrefillP
     const float inv = rsqrtf(ss / 256.0f + p.eps);  // the shader's rsqrt (attention.metal:364-401)
     float n[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) n[i] = x8[i] * inv * bf16_bits_to_f32((wv[i >> 1] >> ((i & 1) * 16)) & 0xffffu);
+    for (int i = 0; i < 8; ++i) {
+      float g = gq[i];
+      if (!is_q) {
+        const float2 g2 = unpack_bf16x2((&kw4.x)[i >> 1]);
+        g = (i & 1) ? g2.y : g2.x;
+      }
+      n[i] = x8[i] * inv * g;
+    }
     float o[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const float partner = __shfl_xor_sync(0xffffffffu, n[i], 4);
-      const float2 cs = *reinterpret_cast<const float2*>(&s_cs[2 * ((lane & 3) * 8 + i)]);
-      const float c = fmaf(cs.x, rot_c, 1.0f - rot_c);  // cos, or 1 on lanes >= 8
-      o[i] = fmaf(partner, cs.y * rot_s, n[i] * c);     // lanes >= 8: n[i] * 1 + partner * 0
+      o[i] = fmaf(partner, rs[i], n[i] * rc[i]);  // lanes >= 8: n * 1 + partner * 0
     }
     const uint4 packed = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
                                     pack_bf16x2(o[6], o[7]));
