@@ -41,7 +41,7 @@ PREFILL_FLOP = 4 * QH * HD * sum(range(1, PREFILL_TOKENS + 1))  # causal-exact Q
 # DRAM bytes of one decode layer call at ctx 32768 (split kernel read 134.30 MB
 # + write 5.93 MB, combine read 8.50 MB), from the ncu capture summarised in
 # profiles/decode_split_kernel_ctx32768.md.
-DECODE_TRAFFIC_32K = 148.73e6
+DECODE_TRAFFIC_32K = 140.24e6
 
 
 def peaks():
