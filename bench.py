@@ -39,8 +39,8 @@ CTX = 32768
 PREFILL_TOKENS, PREFILL_CHUNK = 4096, 512
 PREFILL_FLOP = 4 * QH * HD * sum(range(1, PREFILL_TOKENS + 1))  # causal-exact QK^T + PV
 # DRAM bytes of one decode layer call at ctx 32768 (split kernel read 134.30 MB
-# + write 5.93 MB, combine read 8.50 MB), from the ncu capture summarised in
-# profiles/decode_split_kernel_ctx32768.md.
+# + write 3.46 MB, combine read 2.49 MB), from an ncu capture
+# (dram__bytes_read.sum + dram__bytes_write.sum) of both kernels.
 DECODE_TRAFFIC_32K = 140.24e6
 
 

@@ -12,8 +12,9 @@
  * QwenRunner::encode_attention (src/model/runner.rs:1426-1592),
  * QwenRunner::encode_prefill_attention (runner.rs:1962-2062) and the KV
  * position contract (runner.rs:423-503, 911-944, 2376-2545). Each entry point
- * below names the reference code it replaces. A Rust `extern "C"` block that
- * binds these declarations is given in INTEGRATION.md.
+ * below names the reference code it replaces. A Rust crate binds them with a
+ * plain `extern "C"` block of the same signatures (pointers as *mut/*const,
+ * uint32_t as u32, void* stream as *mut c_void).
  *
  * Conventions
  *   - Every entry point returns an int status (LISA_OK or a negative code).
