@@ -587,13 +587,19 @@ static cudaError_t launch_split(const DecodeParams& p, const CUtensorMap& tk, co
 cudaError_t launch_decode(const DecodeParams& p_in, int rows, const CUtensorMap& tk, const CUtensorMap& tv,
                           int num_sms, cudaStream_t stream) {
   DecodeParams p = p_in;
-  float inv[32];
-  host_inv_freq(inv);
-  for (int r = 0; r < 3; ++r)
+  // inverse frequencies once per process; cos/sin of the f32 angle in double,
+  // for the rows of this call only (host time is part of every layer call)
+  static const struct InvFreqTable {
+    float v[32];
+    InvFreqTable() { host_inv_freq(v); }
+  } inv;
+  for (int r = 0; r < rows && r < 3; ++r)
     for (int j = 0; j < 32; ++j) {
-      const float angle = (float)(p.base + (uint32_t)r) * inv[j];
-      p.rope_c[r][j] = (float)std::cos((double)angle);
-      p.rope_s[r][j] = (float)std::sin((double)angle);
+      const float angle = (float)(p.base + (uint32_t)r) * inv.v[j];
+      double sd, cd;
+      ::sincos((double)angle, &sd, &cd);
+      p.rope_c[r][j] = (float)cd;
+      p.rope_s[r][j] = (float)sd;
     }
   cudaError_t e;
   switch (rows) {
