@@ -459,8 +459,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
       }
       // P = exp2(x * scale*log2e - m), rounded to bf16 and written over the S
       // tile 16 keys at a time so the TMEM stores overlap the exponentials.
-      // 3 of every 8 key pairs are exponentiated on the FMA pipe, the rest on
-      // the SFU, which alone would bound this loop. The denominator sums the
+      // 1 of every 8 key pairs is exponentiated on the FMA pipe, the rest on
+      // the SFU (measured on config 2: 1/8 and 2/8 are equal, 3/8 is 2 % and
+      // 4/8 6 % slower). The denominator sums the
       // f32 values, as the reference's f32 softmax does.
       const float2 cc = make_float2(kLog2Scale, kLog2Scale);
       const float2 nm = make_float2(-mr * kLog2Scale, -mr * kLog2Scale);
@@ -471,7 +472,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           const float2 e = ffma2(make_float2(x[16 * q + 2 * c], x[16 * q + 2 * c + 1]), cc, nm);
-          const float2 pe = c < 3 ? exp2_poly2(e) : make_float2(fast_exp2(e.x), fast_exp2(e.y));
+          const float2 pe = c < 1 ? exp2_poly2(e) : make_float2(fast_exp2(e.x), fast_exp2(e.y));
           pk[c] = pack_bf16x2(pe.x, pe.y);
           if (c & 1) acc1 = fadd2(acc1, pe);
           else acc0 = fadd2(acc0, pe);
