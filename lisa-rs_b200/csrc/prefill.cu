@@ -6,23 +6,29 @@
 //   kv_cache_store_prefill     attention.metal:403-440  -> prefill_prologue_kernel
 //   sdpa_decode_prefill        attention.metal:442-480  -> prefill_attn_kernel
 //   gate_out_bf16              attention.metal:520-531  -> prefill_attn_kernel epilogue
-// The reference scans every key serially per (row, head) on scalar lanes; here
-// a CTA owns 128 query rows of one head and runs a flash-attention loop over
-// 64-key tiles of the causal prefix, with every MMA operand that is reused
-// kept in tensor memory (TMEM, 512 columns):
-//   columns [0,256) O accumulator, [256,384) two S tiles, [384,512) Q (bf16)
-//   warp 0       TMA producer: K/V tiles through a 3-stage ring
-//   warp 1       allocates TMEM, issues tcgen05.mma (one thread):
-//                S_j = Q.K_j^T  (A = Q from TMEM, B = K from smem; M128 N64 K256)
-//                O  += P_j.V_j  (A = P from TMEM, B = V from smem read MN-major;
-//                                M128 N256 K64)
+// The reference scans every key serially per (row, head) on scalar lanes;
+// here a cluster of two CTAs runs a flash-attention loop over 128-key tiles
+// of the causal prefix for 256 query rows of one head, as M=256
+// tcgen05.mma.cta_group::2 tiles issued by rank 0. Each CTA holds 128 rows
+// (its own Q tile in shared memory, its own TMEM: columns [0,256) O,
+// [256,384) and [384,512) two S/P tiles) and loads half of every K tile (64
+// keys) and half of every V tile (128 dims) with one 32 KB TMA box each:
+//   warp 0       Q load, K half-tiles through a 2-slot ring, then the gate tile
+//   warp 2       V half-tiles through a 2-slot ring
+//   warp 1       allocates TMEM; on rank 0 one thread issues
+//                S_j = Q.K_j^T  (A, B from smem; M256 N128 K256)
+//                O  += P_j.V_j  (A = P from TMEM, B = V read MN-major; M256 N256 K128)
+//                in the order S_0, S_1, PV_0, S_2, PV_1, ... without waits
+//                between groups (the next group's inputs are tested before
+//                the current group's last MMA)
 //   warps 4..11  softmax: thread = query row = TMEM lane; warps 4+w and 8+w
-//                share lanes 32w.. and split the columns. They load Q into
-//                TMEM, read S with tcgen05.ld, mask causally, keep an online
-//                max that is only moved (and O rescaled in TMEM) when it grows
-//                by more than 2^8, and write bf16 P over the S tile it came
-//                from; epilogue O/l * sigmoid(gate).
-// Key tiles past the last query row are skipped (causal tile skipping).
+//                share lanes 32w.. and split the columns, exchange their
+//                maxima through shared memory, keep an online max that is only
+//                moved (and O rescaled in TMEM) when it grows by more than 2^8,
+//                and write bf16 P over the S tile it came from; epilogue
+//                O/l * sigmoid(gate) staged in shared memory and written by
+//                one TMA store.
+// Key tiles past the pair's last query row are skipped (causal tile skipping).
 #include <algorithm>
 
 #include "common.cuh"
