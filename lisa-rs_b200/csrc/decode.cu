@@ -9,15 +9,18 @@
 //   gate_out_bf16                     attention.metal:520-531
 //
 // Work decomposition. The KV cache of one layer is [4 kv heads][pos][256] bf16.
-// A work unit is (kv head, 128-token chunk). A persistent CTA owns one kv head
-// (blockIdx & 3) and a strided set of chunks; it streams each chunk's K and V
-// through a 3-stage ring of 16-token tiles with TMA (SWIZZLE_128B boxes, one
-// mbarrier per stage), so the 6 query heads that share the kv head (x rows)
-// read each KV byte from HBM once. One warp per query row:
+// A work unit is (kv head, 448-position chunk). 148 persistent CTAs, 37 per kv
+// head (blockIdx & 3), take chunks from a per-head atomic counter; a
+// producer warp streams each chunk's K and V through a 3-stage ring of
+// 64-position stages (one 32 KB TMA box for K and one for V per stage,
+// 128-byte swizzle, one mbarrier per stage, evict-first L2 hint), so the 6
+// query heads that share the kv head (x rows) read each KV byte from HBM once.
+// Four compute warps per query row, warp w taking positions 16w..16w+15 of a
+// stage for Q.K^T and head dims 64w..64w+63 for P.V:
 //   S^T[16 tok x 8 heads] = K_tile[16 x 256] . Q^T      (mma.m16n8k16, Q in regs)
-//   online softmax per head column (warp shuffles), P rounded to bf16
+//   stage max per head exchanged through shared memory, P rounded to bf16
 //   P^T to B-fragment layout with movmatrix.trans
-//   O^T[256 x 8 heads]   += V_tile^T[256 x 16] . P^T    (mma.m16n8k16)
+//   O^T[64 dims x 8 heads] += V_tile^T[64 x 64] . P^T   (mma.m16n8k16)
 // Heads 6,7 of the 8-wide N dimension are zero padding. The new K/V rows of
 // this call are normalised/roped by the CTA whose chunk holds them, written to
 // the cache and substituted into the staged tile, so the append needs no launch
