@@ -176,6 +176,13 @@ int lisa_attn_decode_window(void* k_cache, void* v_cache, uint32_t window_rows, 
                             const uint16_t* k_norm_w, float eps, float* part_o, float* part_ml,
                             void* workspace, size_t workspace_bytes, void* stream);
 
+/* Device error word of the last lisa_attn_decode_window call that used this
+ * workspace (each call zeroes it first). Synchronises `stream`, returns LISA_OK
+ * or LISA_ETIMEOUT (a bounded device wait of that call gave up: its partials
+ * are not valid) and clears the word. No lisa-rs counterpart (its kernels have
+ * no failure channel). */
+int lisa_attn_window_check_device_error(void* workspace, void* stream);
+
 /* Merge n_parts window partials (stacked: part_o [n_parts][rows][24][256],
  * part_ml [n_parts][rows][24][2]) by log-sum-exp and apply the sigmoid gate
  * taken from q_gate: gated_out bf16 [rows][24*256]. */
@@ -198,12 +205,30 @@ int lisa_attn_merge_windows(int n_parts, int rows, const float* part_o, const fl
  *   - All calls share the one array: calls that can overlap on the GPU (other
  *     streams, other host threads) race; the caller must serialise them.
  * Errors otherwise as lisa_attn_decode (LISA_EINVAL, LISA_ENOSPC when
- * base + rows > capacity). */
+ * base + rows > capacity). A device-side failure (a bounded wait that gave
+ * up) is not visible in the return value, which comes back before the kernels
+ * run: lisa_attn_noalloc_check_device_error reports it. */
 #define LISA_ATTN_NOALLOC_MAX_POSITIONS 16384
 int lisa_attn_decode_noalloc(void* k_cache, void* v_cache, uint32_t capacity, uint32_t base, int rows,
                              int in_dtype, const void* q_gate, const void* k, const void* v,
                              const uint16_t* q_norm_w, const uint16_t* k_norm_w, float eps,
                              uint16_t* gated_out, void* stream);
+
+/* Error word of the last lisa_attn_decode_noalloc call on the current device
+ * (kept in the fixed array, zeroed by every call): synchronises the device,
+ * returns LISA_OK or LISA_ETIMEOUT and clears it. Allocates nothing. */
+int lisa_attn_noalloc_check_device_error(void);
+
+/* ---- test hook ------------------------------------------------------------
+ * No lisa-rs counterpart. Process-wide: every later decode launch (contexts,
+ * windows, no-alloc) gives its bounded mbarrier waits a limit of
+ * wait_limit_us microseconds instead of the default 2 s, and with
+ * withhold_loads != 0 its load warp issues no copy at all, so the compute
+ * warps' first wait runs out, they record LISA_ETIMEOUT in the error word and
+ * return (no copy is in flight, nothing is read or written out of bounds).
+ * lisa_attn_debug_wait_fault(0, 0) restores the defaults. LISA_EINVAL for
+ * withhold_loads without a limit or a limit above 10 s. */
+int lisa_attn_debug_wait_fault(uint32_t wait_limit_us, int withhold_loads);
 
 /* Library build identification (for tests: the .so in use). */
 const char* lisa_attn_build_info(void);

@@ -181,8 +181,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Waits for the phase with the given parity to complete. Gives up after
-// WAIT_LIMIT_NS, records `code` in *err and returns false.
 // Non-blocking probe of the phase; unlike try_wait it costs almost nothing
 // when the phase has already completed.
 __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
@@ -196,13 +194,16 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+// Waits for the phase with the given parity to complete. Gives up after
+// limit_ns of %globaltimer, records `code` in *err and returns false.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
+                                          uint64_t limit_ns = WAIT_LIMIT_NS) {
   if (mbar_test_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   while (true) {
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    if (global_timer_ns() - t0 > WAIT_LIMIT_NS) {
+    if (global_timer_ns() - t0 > limit_ns) {
       if (err) atomicExch(err, code);
       return false;
     }

@@ -29,6 +29,7 @@
 // applies the sigmoid gate.
 #include "common.cuh"
 #include "decode.cuh"
+#include "dispatch.h"
 
 #include <algorithm>
 #include <cmath>
@@ -144,7 +145,7 @@ __global__ void __launch_bounds__(32 * (4 * ROWS + 1), 1)
 
   if (warp == NCOMPUTE) {
     // ---------------- TMA producer ----------------
-    if (lane == 0) {
+    if (lane == 0 && !p.withhold) {
       // The query rows go first, so they are not queued behind the KV ring.
       const uint32_t hb = p.in_bf16 ? 512u : 1024u;  // bytes of one head's 256 query values
       mbar_arrive_expect_tx(qbar, ROWS * GQA * hb + 512);
@@ -166,7 +167,7 @@ __global__ void __launch_bounds__(32 * (4 * ROWS + 1), 1)
         const uint32_t nt = done ? 1 : chunk_tiles(chunk, p.extent);
         for (uint32_t t = 0; t < nt; ++t, ++i) {
           const uint32_t slot = i % DEC_STAGES;
-          if (i >= DEC_STAGES && !mbar_wait(&empty[slot], ((i / DEC_STAGES) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) {
+          if (i >= DEC_STAGES && !mbar_wait(&empty[slot], ((i / DEC_STAGES) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY, p.wait_ns)) {
             done = true;
             break;
           }
@@ -195,7 +196,7 @@ __global__ void __launch_bounds__(32 * (4 * ROWS + 1), 1)
   {
     uint8_t* qrow = smem + DEC_QS_OFF + m * DEC_QROW_BYTES;
     const uint16_t* wn = reinterpret_cast<const uint16_t*>(smem + DEC_WN_OFF);
-    if (!mbar_wait(qbar, 0, p.err, ERR_TIMEOUT_FULL)) return;
+    if (!mbar_wait(qbar, 0, p.err, ERR_TIMEOUT_FULL, p.wait_ns)) return;
     uint4 packed[2];
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
@@ -275,7 +276,7 @@ __global__ void __launch_bounds__(32 * (4 * ROWS + 1), 1)
     const int s = it % DEC_STAGES, par = it & 1;
     uint8_t* stage = smem + s * DEC_STAGE_BYTES;
     DEC_TRACE(0);
-    if (!mbar_wait(&full[s], (it / DEC_STAGES) & 1, p.err, ERR_TIMEOUT_FULL)) return;
+    if (!mbar_wait(&full[s], (it / DEC_STAGES) & 1, p.err, ERR_TIMEOUT_FULL, p.wait_ns)) return;
     DEC_TRACE(1);
     const int code = slot_code[s];
     if (code < 0) break;
@@ -566,13 +567,9 @@ __global__ void __launch_bounds__(256) merge_windows_kernel(int n_parts, int row
 template <int ROWS>
 static cudaError_t launch_split(const DecodeParams& p, const CUtensorMap& tk, const CUtensorMap& tv, int num_sms,
                                 cudaStream_t stream) {
-  static bool configured = false;  // per process; the attribute is per function
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(decode_split_kernel<ROWS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         DEC_SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static SmemAttr attr_once;  // the attribute is per kernel and per device
+  cudaError_t e = attr_once.ensure(decode_split_kernel<ROWS>, DEC_SMEM_BYTES);
+  if (e != cudaSuccess) return e;
   const uint32_t per_head = std::min<uint32_t>(p.nchunks, (uint32_t)(num_sms / KVH));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(per_head * KVH);

@@ -44,6 +44,8 @@ struct DecodeParams {
   float* part_o;         // [rows][4][chunk_cap][256][8] unnormalised sums
   float* part_ml;        // [rows][4][chunk_cap][2][8]  {max, sum}
   int* err;
+  uint64_t wait_ns;      // bounded-wait limit of every mbarrier wait
+  int withhold;          // test hook: the producer issues nothing (waits run out)
   uint32_t* sched;       // [4] per-kv-head chunk counters: zero at launch, reset by the combine
   // RoPE tables filled by launch_decode on the host: cos/sin of rows
   // base..base+2 for the 32 rotated pairs.

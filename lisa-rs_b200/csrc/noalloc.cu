@@ -19,7 +19,7 @@
 #include "../../include/lisa_attn.h"
 #include "common.cuh"
 #include "decode.cuh"
-#include "prefill.cuh"
+#include "dispatch.h"
 
 using namespace lisa;
 
@@ -66,47 +66,39 @@ extern "C" int lisa_attn_decode_noalloc(void* k_cache, void* v_cache, uint32_t c
   if (!k_cache || !v_cache || !q_gate || !k || !v || !q_norm_w || !k_norm_w || !gated_out) return LISA_EINVAL;
   if (rows != 1 && rows != 3) return LISA_EINVAL;
   if (in_dtype != LISA_DTYPE_F32 && in_dtype != LISA_DTYPE_BF16) return LISA_EINVAL;
-  if (capacity == 0 || ((uintptr_t)k_cache & 15) || ((uintptr_t)v_cache & 15)) return LISA_EINVAL;
-  if (((uintptr_t)q_gate & 15) || ((uintptr_t)q_norm_w & 15)) return LISA_EINVAL;
+  if (capacity == 0 || capacity > (1u << 31)) return LISA_EINVAL;  // as lisa_attn_create
+  if (((uintptr_t)k_cache & 15) || ((uintptr_t)v_cache & 15)) return LISA_EINVAL;
   if ((uint64_t)base + rows > capacity) return LISA_ENOSPC;
   if ((uint64_t)base + rows > NOALLOC_MAX_POS) return LISA_E2BIG;  // beyond the fixed scratch
 
   float* scratch = nullptr;
   int s = scratch_for_current_device(&scratch);
   if (s != LISA_OK) return s;
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-
-  DecodeParams p = {};
-  p.q_gate = q_gate;
-  p.k_in = k;
-  p.v_in = v;
-  p.in_bf16 = in_dtype == LISA_DTYPE_BF16;
-  p.q_norm_w = q_norm_w;
-  p.k_norm_w = k_norm_w;
-  p.eps = eps;
-  p.k_cache = static_cast<uint16_t*>(k_cache);
-  p.v_cache = static_cast<uint16_t*>(v_cache);
-  p.window_rows = capacity;
-  p.kv_lo = 0;
-  p.base = base;
-  p.extent = base + (uint32_t)rows;
-  p.nchunks = (p.extent + DEC_CHUNK - 1) / DEC_CHUNK;
-  p.chunk_cap = NOALLOC_CHUNKS;
-  p.part_o = scratch;
-  p.part_ml = scratch + NOALLOC_PO;
-  p.err = reinterpret_cast<int*>(scratch + NOALLOC_PO + NOALLOC_PM);
-  p.sched = reinterpret_cast<uint32_t*>(scratch + NOALLOC_PO + NOALLOC_PM + 16);
-  p.gated_out = gated_out;
-  // Partials are fully written before they are read; the error word and the
-  // chunk counters must start at zero.
+  int* err = reinterpret_cast<int*>(scratch + NOALLOC_PO + NOALLOC_PM);
+  uint32_t* sched = reinterpret_cast<uint32_t*>(scratch + NOALLOC_PO + NOALLOC_PM + 16);
+  // Partials are fully written before they are read; the error word (read
+  // back by lisa_attn_noalloc_check_device_error) and the chunk counters must
+  // start at zero.
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (cudaMemsetAsync(p.err, 0, 128, st) != cudaSuccess) return LISA_ECUDA;
-  CUtensorMap tk, tv;
-  if (lisa_encode_group_map(&tk, k_cache, p.extent, capacity, KVH, DEC_TILE, 4) != LISA_OK ||
-      lisa_encode_group_map(&tv, v_cache, p.extent, capacity, KVH, DEC_TILE, 4) != LISA_OK)
-    return LISA_ECUDA;
-  return launch_decode(p, rows, tk, tv, sms, st) == cudaSuccess ? LISA_OK : LISA_ECUDA;
+  if (cudaMemsetAsync(err, 0, 128, st) != cudaSuccess) return LISA_ECUDA;
+  return run_decode(static_cast<uint16_t*>(k_cache), static_cast<uint16_t*>(v_cache), capacity, 0, base, rows,
+                    in_dtype, q_gate, k, v, q_norm_w, k_norm_w, eps, scratch, scratch + NOALLOC_PO, NOALLOC_CHUNKS,
+                    err, sched, gated_out, nullptr, nullptr, current_device_sms(), st);
+}
+
+// Reads the error word the last lisa_attn_decode_noalloc call on the current
+// device left in the fixed scratch: synchronises the device, returns LISA_OK
+// or LISA_ETIMEOUT (a bounded wait of that call gave up and its output is not
+// valid) and clears the word. Allocates nothing.
+extern "C" int lisa_attn_noalloc_check_device_error(void) {
+  float* scratch = nullptr;
+  int s = scratch_for_current_device(&scratch);
+  if (s != LISA_OK) return s;
+  if (cudaDeviceSynchronize() != cudaSuccess) return LISA_ECUDA;
+  int h = 0;
+  int* err = reinterpret_cast<int*>(scratch + NOALLOC_PO + NOALLOC_PM);
+  if (cudaMemcpy(&h, err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return LISA_ECUDA;
+  if (h && cudaMemset(err, 0, sizeof(int)) != cudaSuccess) return LISA_ECUDA;
+  return h ? LISA_ETIMEOUT : LISA_OK;
 }
 #pragma GCC visibility pop

@@ -33,6 +33,7 @@
 
 #include "common.cuh"
 #include "prefill.cuh"
+#include "dispatch.h"
 #include "tcgen05.cuh"
 
 namespace lisa {
@@ -625,12 +626,9 @@ cudaError_t launch_prefill(const PrefillParams& p_in, int num_sms, cudaStream_t 
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, prefill_prologue_kernel, p);
   if (e != cudaSuccess) return e;
-  static bool configured = false;
-  if (!configured) {
-    e = cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PF_SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static SmemAttr attr_once;  // the attribute is per kernel and per device
+  e = attr_once.ensure(prefill_attn_kernel, PF_SMEM_BYTES);
+  if (e != cudaSuccess) return e;
   CUtensorMap tq, tk, tv, tg = {}, to;
   const uint32_t kv_rows = p.base + (uint32_t)p.rows;
   if (lisa_encode_group_map(&tq, p.q_ws, PF_MAX_ROWS, PF_MAX_ROWS, QH, PF_BM, 4) != 0 ||

@@ -14,12 +14,14 @@
 #include <string.h>
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "../../include/lisa_attn.h"
 #include "decode.cuh"
 #include "prefill.cuh"
 #include "common.cuh"
+#include "dispatch.h"
 
 using namespace lisa;
 
@@ -99,28 +101,27 @@ int lisa_encode_rows_map(CUtensorMap* map, const void* base, uint32_t rows, uint
   return r == CUDA_SUCCESS ? LISA_OK : LISA_ECUDA;
 }
 
+namespace lisa {
+
 namespace {
+std::atomic<uint64_t> g_fault_limit_ns{0};
+std::atomic<int> g_fault_withhold{0};
+}  // namespace
 
-int cuda_status(cudaError_t e) { return e == cudaSuccess ? LISA_OK : LISA_ECUDA; }
+WaitFault current_wait_fault() {
+  return WaitFault{g_fault_limit_ns.load(std::memory_order_relaxed), g_fault_withhold.load(std::memory_order_relaxed)};
+}
 
-size_t layer_elems(const lisa_attn_ctx* c) { return (size_t)KVH * c->capacity * HD; }
+int current_device_sms() {
+  static std::mutex mu;
+  static int sms[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!sms[dev] && cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) sms[dev] = 148;
+  return sms[dev];
+}
 
-bool bad_dtype(int d) { return d != LISA_DTYPE_F32 && d != LISA_DTYPE_BF16; }
-
-struct DeviceGuard {
-  int prev = -1;
-  explicit DeviceGuard(int dev) {
-    cudaGetDevice(&prev);
-    if (prev != dev) cudaSetDevice(dev);
-  }
-  ~DeviceGuard() {
-    int cur = -1;
-    cudaGetDevice(&cur);
-    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
-  }
-};
-
-// Shared decode dispatch for contexts and windows.
 int run_decode(uint16_t* kc, uint16_t* vc, uint32_t window_rows, uint32_t kv_lo, uint32_t base, int rows,
                int in_dtype, const void* q_gate, const void* k, const void* v, const uint16_t* qn,
                const uint16_t* kn, float eps, float* part_o, float* part_ml, uint32_t chunk_cap, int* err,
@@ -145,6 +146,9 @@ int run_decode(uint16_t* kc, uint16_t* vc, uint32_t window_rows, uint32_t kv_lo,
   p.part_o = part_o;
   p.part_ml = part_ml;
   p.err = err;
+  const WaitFault wf = current_wait_fault();
+  p.wait_ns = wf.limit_ns ? wf.limit_ns : WAIT_LIMIT_NS;
+  p.withhold = wf.withhold;
   p.sched = sched;
   p.gated_out = gated;
   p.win_o = win_o;
@@ -156,8 +160,31 @@ int run_decode(uint16_t* kc, uint16_t* vc, uint32_t window_rows, uint32_t kv_lo,
   int s = lisa_encode_group_map(&tk, kc, p.extent, window_rows, KVH, DEC_TILE, 4);
   if (s == LISA_OK) s = lisa_encode_group_map(&tv, vc, p.extent, window_rows, KVH, DEC_TILE, 4);
   if (s != LISA_OK) return s;
-  return cuda_status(launch_decode(p, rows, tk, tv, num_sms, stream));
+  return launch_decode(p, rows, tk, tv, num_sms, stream) == cudaSuccess ? LISA_OK : LISA_ECUDA;
 }
+
+}  // namespace lisa
+
+namespace {
+
+int cuda_status(cudaError_t e) { return e == cudaSuccess ? LISA_OK : LISA_ECUDA; }
+
+size_t layer_elems(const lisa_attn_ctx* c) { return (size_t)KVH * c->capacity * HD; }
+
+bool bad_dtype(int d) { return d != LISA_DTYPE_F32 && d != LISA_DTYPE_BF16; }
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
 
 int check_layer_args(lisa_attn_ctx* c, int layer, int in_dtype, const void* q_gate, const void* k, const void* v,
                      const uint16_t* qn, const uint16_t* kn, const void* out) {
@@ -182,7 +209,7 @@ int lisa_attn_create(int device, int n_layers, uint32_t capacity, lisa_attn_ctx*
   c->n_layers = n_layers;
   c->capacity = capacity;
   c->chunk_cap = (capacity + DEC_CHUNK - 1) / DEC_CHUNK;
-  cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device);
+  c->num_sms = current_device_sms();
   const size_t cache_bytes = (size_t)n_layers * layer_elems(c) * sizeof(uint16_t);
   const size_t po = (size_t)MAX_DECODE_ROWS * KVH * c->chunk_cap * 2048 * sizeof(float);
   const size_t pm = (size_t)MAX_DECODE_ROWS * KVH * c->chunk_cap * 16 * sizeof(float);
@@ -370,12 +397,15 @@ int lisa_attn_check_device_error(lisa_attn_ctx* c) {
   return h ? LISA_ETIMEOUT : LISA_OK;
 }
 
+// Window workspace layout: [0, 256) the device error word (offset 0) and the
+// four chunk counters (offset 64); then the chunk partials O and (max, sum),
+// each 256-byte aligned.
 size_t lisa_attn_window_workspace_bytes(uint32_t window_rows, int rows) {
   if (window_rows == 0 || rows < 1 || rows > MAX_DECODE_ROWS) return 0;
   const size_t chunks = (window_rows + DEC_CHUNK - 1) / DEC_CHUNK;
   const size_t po = (size_t)rows * KVH * chunks * 2048 * sizeof(float);
   const size_t pm = (size_t)rows * KVH * chunks * 16 * sizeof(float);
-  return ((po + 255) & ~size_t(255)) + ((pm + 255) & ~size_t(255)) + 256;
+  return 256 + ((po + 255) & ~size_t(255)) + ((pm + 255) & ~size_t(255));
 }
 
 int lisa_attn_decode_window(void* k_cache, void* v_cache, uint32_t window_rows, uint32_t kv_lo, uint32_t base,
@@ -386,24 +416,42 @@ int lisa_attn_decode_window(void* k_cache, void* v_cache, uint32_t window_rows, 
     return LISA_EINVAL;
   if (!q_gate || !k || !v || !qn || !kn || !part_o || !part_ml || !workspace) return LISA_EINVAL;
   if (((uintptr_t)workspace & 255) || ((uintptr_t)k_cache & 15) || ((uintptr_t)v_cache & 15)) return LISA_EINVAL;
+  if (window_rows > (1u << 31)) return LISA_EINVAL;  // row stride limit of the tensor maps
   const size_t need = lisa_attn_window_workspace_bytes(window_rows, rows);
   if (workspace_bytes < need) return LISA_EINVAL;
   if ((uint64_t)base + rows > (uint64_t)1 << 31) return LISA_ENOSPC;
   const uint32_t chunks = (window_rows + DEC_CHUNK - 1) / DEC_CHUNK;
   const size_t po = (size_t)rows * KVH * chunks * 2048 * sizeof(float);
-  const size_t pm = (size_t)rows * KVH * chunks * 16 * sizeof(float);
   uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
-  float* wo = reinterpret_cast<float*>(ws);
-  float* wm = reinterpret_cast<float*>(ws + ((po + 255) & ~size_t(255)));
-  int* err = reinterpret_cast<int*>(ws + ((po + 255) & ~size_t(255)) + ((pm + 255) & ~size_t(255)));
-  uint32_t* sched = reinterpret_cast<uint32_t*>(err + 16);
-  // error word and chunk counters start at zero
-  if (cudaMemsetAsync(err, 0, 128, (cudaStream_t)stream) != cudaSuccess) return LISA_ECUDA;
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int* err = reinterpret_cast<int*>(ws);
+  uint32_t* sched = reinterpret_cast<uint32_t*>(ws + 64);
+  float* wo = reinterpret_cast<float*>(ws + 256);
+  float* wm = reinterpret_cast<float*>(ws + 256 + ((po + 255) & ~size_t(255)));
+  // The error word (read back by lisa_attn_window_check_device_error) and the
+  // chunk counters start at zero on every call.
+  if (cudaMemsetAsync(ws, 0, 128, (cudaStream_t)stream) != cudaSuccess) return LISA_ECUDA;
   return run_decode((uint16_t*)k_cache, (uint16_t*)v_cache, window_rows, kv_lo, base, rows, in_dtype, q_gate, k, v,
-                    qn, kn, eps, wo, wm, chunks, err, sched, nullptr, part_o, part_ml, sms, (cudaStream_t)stream);
+                    qn, kn, eps, wo, wm, chunks, err, sched, nullptr, part_o, part_ml, current_device_sms(),
+                    (cudaStream_t)stream);
+}
+
+int lisa_attn_window_check_device_error(void* workspace, void* stream) {
+  if (!workspace || ((uintptr_t)workspace & 255)) return LISA_EINVAL;
+  int h = 0;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (cudaMemcpyAsync(&h, workspace, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return LISA_ECUDA;
+  if (h && cudaMemsetAsync(workspace, 0, sizeof(int), st) != cudaSuccess) return LISA_ECUDA;
+  return h ? LISA_ETIMEOUT : LISA_OK;
+}
+
+int lisa_attn_debug_wait_fault(uint32_t wait_limit_us, int withhold_loads) {
+  if (withhold_loads && wait_limit_us == 0) return LISA_EINVAL;  // a withheld load needs a short limit
+  if (wait_limit_us > 10u * 1000u * 1000u) return LISA_EINVAL;
+  g_fault_limit_ns.store((uint64_t)wait_limit_us * 1000u, std::memory_order_relaxed);
+  g_fault_withhold.store(withhold_loads ? 1 : 0, std::memory_order_relaxed);
+  return LISA_OK;
 }
 
 int lisa_attn_merge_windows(int n_parts, int rows, const float* part_o, const float* part_ml, int in_dtype,
@@ -416,7 +464,7 @@ int lisa_attn_merge_windows(int n_parts, int rows, const float* part_o, const fl
 }
 
 const char* lisa_attn_build_info(void) {
-  return "lisa_attn sm_100a: split-KV decode (mma.sync + TMA), tcgen05 prefill; chunk 128";
+  return "lisa_attn sm_100a: split-KV decode (mma.sync + TMA ring, 448-position chunks), tcgen05 cta_group::2 prefill";
 }
 
 }  // extern "C"

@@ -55,7 +55,10 @@ SIGNATURES = {
     "lisa_attn_decode_window": (_i32, [_P, _P, _u32, _u32, _u32, _i32, _i32, _P, _P, _P, _P, _P, _f32, _P, _P,
                                        _P, _sz, _P]),
     "lisa_attn_merge_windows": (_i32, [_i32, _i32, _P, _P, _i32, _P, _P, _P]),
+    "lisa_attn_window_check_device_error": (_i32, [_P, _P]),
     "lisa_attn_decode_noalloc": (_i32, [_P, _P, _u32, _u32, _i32, _i32, _P, _P, _P, _P, _P, _f32, _P, _P]),
+    "lisa_attn_noalloc_check_device_error": (_i32, []),
+    "lisa_attn_debug_wait_fault": (_i32, [_u32, _i32]),
     "lisa_attn_build_info": (ctypes.c_char_p, []),
 }
 
@@ -281,6 +284,13 @@ def decode_window(k_cache, v_cache, kv_lo, base, rows, q_gate, k, v, w, part_o, 
                                        _dtype_code(q_gate), _ptr(q_gate), _ptr(k), _ptr(v), _ptr(w.q_norm),
                                        _ptr(w.k_norm), eps, _ptr(part_o), _ptr(part_ml), _ptr(workspace),
                                        workspace.numel() * workspace.element_size(), _stream_ptr(stream)))
+
+
+def window_check_device_error(workspace, stream=None):
+    """Raises LisaError(ETIMEOUT) if the last decode_window call on this
+    workspace had a device wait give up."""
+    _check("lisa_attn_window_check_device_error",
+           load_library().lisa_attn_window_check_device_error(_ptr(workspace), _stream_ptr(stream)))
 
 
 def merge_windows(n_parts, rows, part_o, part_ml, q_gate, out, stream=None):
