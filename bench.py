@@ -12,8 +12,14 @@ reports it under "prefill".
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                   [--workload decode32k|batched|longctx]
 
-N > 1 runs under torchrun, one rank per GPU; decode32k shards independent
-sequences (one per rank, weak scaling, no collective).
+N > 1 runs under torchrun, one rank per GPU. The headline decode32k gives
+every rank its own sequence (weak scaling, no collective) and reports the
+per-GPU µs per layer call of the slowest rank. The same line carries, at every
+N, the two multi-GPU splits of the path as nested blocks: "batched" (config 3,
+64 sequences sharded over the GPUs, strong scaling) and "longctx" /
+"longctx_m3" (config 4, one 262144-position sequence whose KV is split over
+the GPUs, partials exchanged through peer memory, strong scaling), each with
+its roofline against N x the measured HBM bandwidth.
 """
 from __future__ import annotations
 
@@ -42,6 +48,7 @@ PREFILL_FLOP = 4 * QH * HD * sum(range(1, PREFILL_TOKENS + 1))  # causal-exact Q
 # + write 3.46 MB, combine read 2.49 MB), from an ncu capture
 # (dram__bytes_read.sum + dram__bytes_write.sum) of both kernels.
 DECODE_TRAFFIC_32K = 140.24e6
+DECODE_TRAFFIC_SOURCE = "ncu capture of both kernels at commit e1fb7d8 (kernels unchanged since in their data path)"
 
 
 def peaks():
@@ -382,43 +389,54 @@ def fill_random(t, gen):
         k += 1
 
 
-def bench_longctx(args, rank, world, local):
-    """one sequence of 262144 positions, M=1 decode of one
-    layer, KV split over the ranks (lisa_split windows) with one all-gather of
-    partials per step. Strong scaling: value = µs per decode step."""
+def bench_longctx(args, rank, world, local, rows=1):
+    """one sequence of 262144 positions, one layer, M=1
+    (new row at 262143) or the M=3 verify variant (rows at 262141..262143);
+    the KV is split into one window per rank (lisa_split.plan_windows) and the
+    window partials are exchanged through peer memory inside the step
+    (lisa_attn_xchg_decode: split kernel, publishing combine, bounded-wait
+    merge). The step is captured in a CUDA graph. Strong scaling: the job is
+    one decode step whatever the number of GPUs."""
     import torch
 
-    import lisa_attn
     import lisa_split
 
     cap = 262144
-    base = cap - 1
+    base = cap - rows
     stream = torch.cuda.current_stream()
     gen = torch.Generator(device="cuda")
     gen.manual_seed(0x5EED + 4 + rank)
     win = lisa_split.plan_windows(cap, world)[rank]
-    dec = lisa_split.SplitKVDecoder(win, max_rows=1)
+    dec = lisa_split.SplitKVDecoder(win, max_rows=3)
     fill_random(dec.k, gen)
     fill_random(dec.v, gen)
     w = make_weights(gen, 1)[0]
     g0 = torch.Generator(device="cuda")
-    g0.manual_seed(0x5EED)  # identical inputs on every rank
-    q = torch.randn((1, QROW), generator=g0, device="cuda")
-    k = torch.randn((1, KROW), generator=g0, device="cuda")
-    v = torch.randn((1, KROW), generator=g0, device="cuda")
-    out = torch.empty((1, OROW), dtype=torch.bfloat16, device="cuda")
-
-    def step():
+    g0.manual_seed(0x5EED + rows)  # identical inputs on every rank
+    q = torch.randn((rows, QROW), generator=g0, device="cuda")
+    k = torch.randn((rows, KROW), generator=g0, device="cuda")
+    v = torch.randn((rows, KROW), generator=g0, device="cuda")
+    out = torch.empty((rows, OROW), dtype=torch.bfloat16, device="cuda")
+    # warm up eagerly, then capture one step (every rank does the same count
+    # of steps: each one is an exchange all ranks take part in)
+    for _ in range(3):
         dec.decode(base, q, k, v, w, out, stream)
-
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    cs = torch.cuda.Stream()
+    with torch.cuda.stream(cs):
+        with torch.cuda.graph(graph, stream=cs):
+            dec.decode(base, q, k, v, w, out, cs)
+    torch.cuda.synchronize()
+    barrier(world)
     with ClockSampler(local) as clk:
-        t_end = time.perf_counter() + 1.0
-        while time.perf_counter() < t_end:
-            for _ in range(10):
-                step()
-            torch.cuda.synchronize()
-        ms = timed(step, args.steps, args.warmup, world, stream)
-    return {"ms": ms, "clocks": clk.summary(), "bytes": 4096 * cap}
+        for _ in range(200):  # a fixed count, identical on every rank
+            graph.replay()
+        torch.cuda.synchronize()
+        ms = timed(graph.replay, args.steps, args.warmup, world, stream)
+    dec.check_device_error()
+    return {"ms": ms, "clocks": clk.summary(), "bytes": 4096 * cap + rows * (QROW * 4 + 2 * KROW * 4 + OROW * 2),
+            "per_gpu_bytes_max": 4096 * max(w_.rows for w_ in lisa_split.plan_windows(cap, world))}
 
 
 def bench_batched(args, rank, world, local):
@@ -476,7 +494,8 @@ def bench_batched(args, rank, world, local):
     with ClockSampler(local) as clk:
         ms = timed(step, args.steps, args.warmup, world, stream)
     total_ctx = sum(ctx)
-    return {"ms": ms, "clocks": clk.summary(), "bytes": 4096 * total_ctx * LAYERS, "ctx_sum": total_ctx}
+    return {"ms": ms, "clocks": clk.summary(), "bytes": 4096 * total_ctx * LAYERS, "ctx_sum": total_ctx,
+            "launches": 2 * LAYERS * len(runners)}
 
 
 def emit(line: dict) -> None:
@@ -518,6 +537,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode32k", choices=["decode32k", "batched", "longctx"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--decode-only", action="store_true", help="skip the batched / longctx blocks")
+    ap.add_argument("--rows", type=int, default=1, choices=[1, 3], help="rows of --workload longctx")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -531,58 +552,97 @@ def main():
 
     rank, world, local = dist_setup()
     pk = peaks()
+    hbm_job = pk["hbm_gbs"] * world
+
+    def split_block(r, kind):
+        """Nested line of a multi-GPU split (config 3 or 4): whole-job time,
+        roofline against world x measured HBM."""
+        step_us = r["ms"] * 1000.0 / args.steps
+        gbs = r["bytes"] / (step_us * 1e-6) / 1e9
+        blk = {"ms_per_step": round(step_us / 1000, 4), "higher_is_better": False, "scaling": "strong",
+               "n_gpus": world, "clocks": r["clocks"],
+               "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": round(hbm_job, 1), "unit": "GB/s",
+                            "frac": round(gbs / hbm_job, 4), "traffic": None, "peak_source": pk["source"],
+                            "note": f"whole job: algorithmic bytes / step time, peak = {world} x measured HBM"}}
+        if kind == "batched":
+            blk.update({"workload": "config 3: 64 sequences, ctx U[1024,32768] seeded (sum %d), 16 attention "
+                                    "layers, M=1; sequences sharded over the GPUs, no collective; one CUDA graph "
+                                    "per step" % r["ctx_sum"],
+                        "value": round(step_us / LAYERS, 3), "unit": "µs/layer (all 64 sequences)",
+                        "launches_per_step": r["launches"]})
+        else:
+            blk.update({"workload": "config 4: one sequence, ctx 262144, rows %d; KV split into one window per "
+                                    "GPU, window partials exchanged by peer stores + bounded-wait merge inside the "
+                                    "step (no collective library call); one CUDA graph per step" % r["rows"],
+                        "value": round(step_us, 3), "unit": "µs/step (one layer)",
+                        "per_gpu_kv_bytes": r["per_gpu_bytes_max"]})
+        return blk
+
     if args.workload in ("batched", "longctx"):
-        fn = bench_batched if args.workload == "batched" else bench_longctx
-        r = fn(args, rank, world, local)
+        r = bench_batched(args, rank, world, local) if args.workload == "batched" else \
+            bench_longctx(args, rank, world, local, rows=args.rows)
+        if args.workload == "longctx":
+            r["rows"] = args.rows
         if rank == 0:
-            step_us = r["ms"] * 1000.0 / args.steps
-            value = step_us / LAYERS if args.workload == "batched" else step_us
-            gbs = r["bytes"] / (step_us * 1e-6) / 1e9
-            emit({"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
-                  "warmup": args.warmup, "ms_per_step": round(step_us / 1000, 4), "higher_is_better": False,
+            blk = split_block(r, args.workload)
+            emit({"metric": METRIC, "value": blk["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                  "warmup": args.warmup, "ms_per_step": blk["ms_per_step"], "higher_is_better": False,
                   "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-                  "config": {"workload": args.workload + (
-                      ": config 3, 64 sequences ctx U[1024,32768] (sum %d), 16 layers, sequences sharded, one CUDA graph per step"
-                      % r["ctx_sum"] if args.workload == "batched" else
-                      ": config 4, ctx 262144 M=1, KV split over ranks, one all-gather of partials"),
-                      "parallelism": f"{world} ranks"},
-                  "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"] * world,
-                               "unit": "GB/s", "frac": round(gbs / (pk["hbm_gbs"] * world), 4), "traffic": None,
-                               "peak_source": pk["source"], "note": "whole job, peak = ranks x measured HBM"},
-                  "clocks": r["clocks"]})
+                  "config": {"workload": blk["workload"], "parallelism": f"{world} ranks"},
+                  "roofline": blk["roofline"], "clocks": blk["clocks"]})
         if world > 1:
             import torch.distributed as dist
 
             dist.destroy_process_group()
         return
+
     r = bench_decode32k(args, rank, world, local)
+    torch.cuda.empty_cache()
     pf_ms, pf_ms_eager = bench_prefill(args, world)
+    torch.cuda.empty_cache()
+    blocks = {}
+    if not args.decode_only:
+        rb = bench_batched(args, rank, world, local)
+        blocks["batched"] = split_block(rb, "batched")
+        torch.cuda.empty_cache()
+        for rows in (1, 3):
+            rl = bench_longctx(args, rank, world, local, rows=rows)
+            rl["rows"] = rows
+            blocks["longctx" if rows == 1 else "longctx_m3"] = split_block(rl, "longctx")
+            torch.cuda.empty_cache()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         us, nthr, reps = cpu_baseline_decode(seconds=10.0)
         cpu = {"value": round(us, 2), "unit": UNIT, "cores": nthr, "kind": "port",
                "sample": f"{reps} oracle runs of one M=1 decode layer at ctx {CTX} (median)"}
     if rank != 0:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
         return
-    layers_total = LAYERS * world
-    value = r["ms"] * 1000.0 / args.steps / layers_total  # aggregate µs per sequence-layer
-    e2e = r["ms_e2e"] * 1000.0 / args.steps / layers_total
+    # per-GPU figures: every rank decodes its own 32K sequence (weak scaling),
+    # the slowest rank's time is reported
+    value = r["ms"] * 1000.0 / args.steps / LAYERS  # µs per layer call on one GPU
+    e2e = r["ms_e2e"] * 1000.0 / args.steps / LAYERS
     layer_bytes = decode_bytes(CTX, 1)
     # average duration of one layer call (split + combine) over the timed
     # region: K steps x 16 back-to-back calls, CUDA events on the stream
     achieved = layer_bytes / (value * 1e-6) / 1e9
     pf_tflops = PREFILL_FLOP / (pf_ms / args.steps * 1e-3) / 1e12
-    emit({
+    line = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(r["ms"] / args.steps, 4), "higher_is_better": False,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": "decode32k: M=1 decode, ctx 32768, 16 stacked attention layers per step, "
-                               "one sequence per GPU, step replayed as a CUDA graph", "ctx": CTX, "rows": 1, "layers": LAYERS,
+                               "one sequence per GPU (value = per-GPU µs per layer call, slowest rank), "
+                               "step replayed as a CUDA graph", "ctx": CTX, "rows": 1, "layers": LAYERS,
                    "sequences": world, "parallelism": f"sequences sharded, dp{world}, no collective",
                    "l2": "inputs larger than L2 (16 x 134 MB KV per step)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": DECODE_TRAFFIC_32K, "peak_source": pk["source"],
-                     "kernel": "decode_split_kernel<1> + decode_combine_kernel (one layer call)",
+                     "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": DECODE_TRAFFIC_32K,
+                     "traffic_source": DECODE_TRAFFIC_SOURCE, "peak_source": pk["source"],
+                     "kernel": "decode_split_kernel<1> + decode_combine_kernel (one layer call, one GPU)",
                      "algorithmic_bytes": layer_bytes, "layer_us_timed": round(value, 3),
                      "layer_us_isolated": round(r["layer_ms"] * 1000, 3)},
         "cpu_baseline": cpu,
@@ -599,7 +659,9 @@ def main():
                                  "unit": "TFLOP/s", "frac": round(pf_tflops / pk["bf16_tflops"], 4), "traffic": None,
                                  "kernel": "prefill_prologue_kernel + prefill_attn_kernel, 8 chunk calls"},
                     "gpu_launches_per_step": 2 * (PREFILL_TOKENS // PREFILL_CHUNK)},
-    })
+    }
+    line.update(blocks)
+    emit(line)
     if world > 1:
         import torch.distributed as dist
 

@@ -189,6 +189,44 @@ int lisa_attn_window_check_device_error(void* workspace, void* stream);
 int lisa_attn_merge_windows(int n_parts, int rows, const float* part_o, const float* part_ml,
                             int in_dtype, const void* q_gate, uint16_t* gated_out, void* stream);
 
+/* ---- split-KV decode with a peer-memory exchange (multi-GPU) ---------------
+ * No lisa-rs counterpart (lisa-rs drives one GPU). One long sequence's KV is
+ * split into contiguous windows, one per rank (one process per GPU, the GPUs
+ * of one node, world <= 8). Per step every rank runs lisa_attn_xchg_decode on
+ * its window with the same inputs: the split kernel streams the window, the
+ * combine kernel writes the window's per-(row, head) partial (normalised O,
+ * max, sum) into every rank's receive region with peer stores and raises
+ * release flags there, and a merge kernel waits (bounded) for all ranks'
+ * flags, merges the partials by log-sum-exp in rank order and applies the
+ * gate, so every rank ends with the same gated_out. The merge of
+ * sdpa_decode_final (attention.metal:611-641), taken across GPUs.
+ * Setup: every rank calls lisa_attn_xchg_create, exports its receive region
+ * with lisa_attn_xchg_handle (LISA_ATTN_XCHG_HANDLE_BYTES bytes, a CUDA IPC
+ * handle), the caller all-gathers the handles in rank order (any host
+ * transport), and every rank calls lisa_attn_xchg_open with the world's
+ * handles before the first step. All ranks must make the same sequence of
+ * lisa_attn_xchg_decode calls (same rows), as they would of a collective.
+ * The step counter is kept on the device, so a step can be captured in a CUDA
+ * graph and replayed. A rank whose peer never delivers gets LISA_ETIMEOUT from
+ * lisa_attn_xchg_check_device_error (the merge's wait gives up after 2 s). */
+#define LISA_ATTN_XCHG_HANDLE_BYTES 64
+#define LISA_ATTN_XCHG_MAX_WORLD 8
+typedef struct lisa_attn_xchg lisa_attn_xchg;
+/* window_rows: positions this rank's window holds; max_rows: 1 or 3. */
+int lisa_attn_xchg_create(int device, int world, int rank, int max_rows, uint32_t window_rows,
+                          lisa_attn_xchg** out);
+int lisa_attn_xchg_handle(lisa_attn_xchg* x, void* handle_out);
+int lisa_attn_xchg_open(lisa_attn_xchg* x, const void* handles);
+/* k_cache / v_cache: this rank's window, [4][window_rows][256] bf16, row i =
+ * position kv_lo + i. rows 1 or 3 (<= max_rows). LISA_ESTATE before open. */
+int lisa_attn_xchg_decode(lisa_attn_xchg* x, void* k_cache, void* v_cache, uint32_t kv_lo, uint32_t base, int rows,
+                          int in_dtype, const void* q_gate, const void* k, const void* v, const uint16_t* q_norm_w,
+                          const uint16_t* k_norm_w, float eps, uint16_t* gated_out, void* stream);
+/* Synchronises `stream`; LISA_ETIMEOUT if a bounded wait of an earlier step
+ * (this rank's split kernel, or the merge waiting for a peer) gave up; clears. */
+int lisa_attn_xchg_check_device_error(lisa_attn_xchg* x, void* stream);
+int lisa_attn_xchg_destroy(lisa_attn_xchg* x);
+
 /* ---- decode without allocation -------------------------------------------
  * No counterpart in lisa-rs. For callers that may not allocate device memory
  * while they run: an engine that hands out all of its GPU memory from a pool

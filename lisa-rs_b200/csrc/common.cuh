@@ -30,6 +30,7 @@ constexpr float SCALE = 0.0625f;  // 1/sqrt(256)
 constexpr int ERR_TIMEOUT_FULL = 1;
 constexpr int ERR_TIMEOUT_EMPTY = 2;
 constexpr int ERR_TIMEOUT_MMA = 3;
+constexpr int ERR_TIMEOUT_XCHG = 4;  // a peer's partials did not arrive
 
 // Bounded waits give up after this many nanoseconds of %globaltimer.
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;
@@ -208,6 +209,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
       return false;
     }
   }
+}
+
+// ---- system-scope flags (peer memory over NVLink) ----------------------------
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
 // Order this thread's generic-proxy shared-memory writes before later

@@ -519,6 +519,38 @@ __global__ void __launch_bounds__(CMB_THREADS) decode_combine_kernel(const Decod
     __syncthreads();
   }
   if (phase != 0) return;
+  if (p.xchg) {
+    // Exchange mode: this CTA's slice of the window partial (row m, kv head,
+    // 8 dims, 6 heads) goes to every rank's receive region (peer stores over
+    // NVLink), then one release flag per destination says it is there.
+    const XchgDev& x = *p.xchg;
+    const uint32_t epoch = x.state[0] + 1;
+    const size_t xs = (size_t)(epoch & 1) * x.world + x.rank;  // parity, source rank
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int hl = 2 * hp + e;
+      if (hl >= GQA) continue;
+      const int h = kvh * GQA + hl;
+      const float a = e ? st.a1 : st.a0, dn = e ? st.d1 : st.d0, gmax = e ? st.m1 : st.m0;
+      const float o = nch ? a / dn : 0.f;
+      const size_t rec = ((xs * x.max_rows + m) * QH + h) * XCHG_REC;
+      for (int dst = 0; dst < x.world; ++dst) {
+        float* r = x.recv[dst] + rec;
+        r[dim] = o;
+        if (dim == 0) {
+          r[HD] = nch ? gmax : -INFINITY;
+          r[HD + 1] = nch ? dn : 0.f;
+        }
+      }
+    }
+    __syncwarp();
+    if (slot == 0) {
+      __threadfence_system();
+      const size_t f = (((size_t)x.rank * 3 + m) * KVH + kvh) * 32 + db;
+      for (int dst = 0; dst < x.world; ++dst) st_release_sys(x.flags[dst] + f, epoch);
+    }
+    return;
+  }
 #pragma unroll
   for (int e = 0; e < 2; ++e) {
     const int hl = 2 * hp + e;
@@ -562,6 +594,69 @@ __global__ void __launch_bounds__(256) merge_windows_kernel(int n_parts, int row
   const float gv = load_in_bf16(q_gate, (size_t)m * QROW + (size_t)h * 512 + 256 + d, in_bf16);
   const float sg = 1.0f / (1.0f + exp2f(-LOG2E * gv));
   gated_out[(size_t)m * OROW + h * HD + d] = f32_to_bf16_bits(o * sg);
+}
+
+// Exchange merge: grid rows * 24 CTAs (row m, head h) of 256 threads (one per
+// dim). Threads 0 .. 32*world-1 wait (bounded, acquire loads at system scope)
+// for the flags of the 32 dim blocks of kv head h/6 from every rank; then the
+// world partials are merged by log-sum-exp in rank order (the same order on
+// every rank, so every rank produces identical bits) and gated. The last CTA
+// to finish advances the step counter.
+__global__ void __launch_bounds__(256) merge_exchange_kernel(const XchgDev* xp, int rows, int in_bf16,
+                                                             const void* q_gate, uint16_t* gated_out,
+                                                             uint64_t wait_ns) {
+  pdl_wait_primary();
+  const XchgDev& x = *xp;
+  const int mh = blockIdx.x;
+  const int m = mh / QH, h = mh % QH, d = threadIdx.x, kvh = h / GQA;
+  const uint32_t epoch = x.state[0] + 1;
+  __shared__ int s_fail;
+  if (threadIdx.x == 0) s_fail = 0;
+  __syncthreads();
+  if (threadIdx.x < 32 * x.world) {
+    const int src = threadIdx.x >> 5, db = threadIdx.x & 31;
+    const uint32_t* f = x.flags[x.rank] + (((size_t)src * 3 + m) * KVH + kvh) * 32 + db;
+    if ((int32_t)(ld_acquire_sys(f) - epoch) < 0) {
+      const uint64_t t0 = global_timer_ns();
+      while ((int32_t)(ld_acquire_sys(f) - epoch) < 0) {
+        if (global_timer_ns() - t0 > wait_ns) {
+          atomicExch(reinterpret_cast<int*>(x.state + 2), ERR_TIMEOUT_XCHG);
+          s_fail = 1;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+  }
+  __syncthreads();
+  if (!s_fail) {
+    const float* base = x.recv[x.rank] + (size_t)(epoch & 1) * x.world * x.max_rows * QH * XCHG_REC;
+    float gmax = -INFINITY;
+    for (int g = 0; g < x.world; ++g)
+      gmax = fmaxf(gmax, __ldcv(base + (((size_t)g * x.max_rows + m) * QH + h) * XCHG_REC + HD));
+    float acc = 0.f, den = 0.f;
+    for (int g = 0; g < x.world; ++g) {
+      const float* r = base + (((size_t)g * x.max_rows + m) * QH + h) * XCHG_REC;
+      const float lg = __ldcv(r + HD + 1);
+      if (lg == 0.f) continue;
+      const float w = exp2f(LOG2E * (__ldcv(r + HD) - gmax)) * lg;
+      acc += w * __ldcv(r + d);
+      den += w;
+    }
+    const float o = den > 0.f ? acc / den : 0.f;
+    const float gv = load_in_bf16(q_gate, (size_t)m * QROW + (size_t)h * 512 + 256 + d, in_bf16);
+    const float sg = 1.0f / (1.0f + exp2f(-LOG2E * gv));
+    gated_out[(size_t)m * OROW + h * HD + d] = f32_to_bf16_bits(o * sg);
+  }
+  // every CTA has read the step counter before the last one advances it
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(x.state + 1, 1u) == gridDim.x - 1) {
+      x.state[1] = 0;
+      x.state[0] = epoch;
+    }
+  }
 }
 
 template <int ROWS>
@@ -620,6 +715,20 @@ cudaError_t launch_decode(const DecodeParams& p_in, int rows, const CUtensorMap&
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, decode_combine_kernel, p);
+}
+
+cudaError_t launch_merge_exchange(const XchgDev* x, int rows, int in_bf16, const void* q_gate, uint16_t* gated_out,
+                                  uint64_t wait_ns, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(rows * QH);
+  cfg.blockDim = dim3(HD);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, merge_exchange_kernel, x, rows, in_bf16, q_gate, gated_out, wait_ns);
 }
 
 cudaError_t launch_merge_windows(int n_parts, int rows, const float* part_o, const float* part_ml, int in_bf16,

@@ -24,6 +24,23 @@ constexpr int DEC_SMEM_BYTES = DEC_WN_OFF + 512 + 1024;
 constexpr int CMB_DIMS_PER_CTA = 8;
 constexpr int CMB_PHASES = 32;
 constexpr int CMB_THREADS = 32 * CMB_PHASES;
+constexpr int HD_FLOATS_PLUS_ML = 256 + 2;
+
+// Window-partial exchange between the ranks of one split-KV sequence (one
+// GPU per rank, peer memory mapped by CUDA IPC). Lives in device memory.
+constexpr int XCHG_MAX_WORLD = 8;
+constexpr int XCHG_REC = HD_FLOATS_PLUS_ML;  // floats per (row, head) record: O[256], max, sum
+struct XchgDev {
+  float* recv[XCHG_MAX_WORLD];      // receive region of rank i, as mapped in this process
+  uint32_t* flags[XCHG_MAX_WORLD];  // flag array of rank i, as mapped in this process
+  uint32_t* state;                  // this rank: [0] completed exchanges, [1] merge CTAs done, [2] error word
+  int world, rank, max_rows;
+};
+// recv[parity][src rank][row][24 heads][XCHG_REC] floats; flags[src][row][kv head][32 dim blocks]
+__host__ __device__ constexpr size_t xchg_recv_floats(int world, int max_rows) {
+  return (size_t)2 * world * max_rows * 24 * XCHG_REC;
+}
+__host__ __device__ constexpr size_t xchg_flag_words(int world) { return (size_t)world * 3 * 4 * 32; }
 
 struct DecodeParams {
   const void* q_gate;  // [rows][24][512]
@@ -55,6 +72,7 @@ struct DecodeParams {
   uint16_t* gated_out;
   float* win_o;   // [rows][24][256]
   float* win_ml;  // [rows][24][2]
+  const XchgDev* xchg;  // or: publish the window partials to every rank (exchange mode)
 #ifdef LISA_DECODE_TRACE
   unsigned long long* trace;  // debug builds only: per-phase cycle totals
 #endif
@@ -65,6 +83,12 @@ struct DecodeParams {
 // {256, extent, 4} with SWIZZLE_128B boxes of {64, 16, 1}.
 cudaError_t launch_decode(const DecodeParams& p, int rows, const CUtensorMap& tk, const CUtensorMap& tv,
                           int num_sms, cudaStream_t stream);
+
+// Exchange mode: waits (bounded) for every rank's window partials of this
+// step, merges them by log-sum-exp and applies the gate; then advances the
+// exchange step counter.
+cudaError_t launch_merge_exchange(const XchgDev* x, int rows, int in_bf16, const void* q_gate,
+                                  uint16_t* gated_out, uint64_t wait_ns, cudaStream_t stream);
 
 // Merges n_parts window partials and applies the gate.
 cudaError_t launch_merge_windows(int n_parts, int rows, const float* part_o, const float* part_ml,

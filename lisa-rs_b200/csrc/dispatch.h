@@ -9,6 +9,8 @@
 #include <atomic>
 #include <mutex>
 
+#include "decode.cuh"
+
 namespace lisa {
 
 // Split-KV decode of `rows` query rows over one cache window (a context's
@@ -16,12 +18,14 @@ namespace lisa {
 // and launches the split kernel plus its combine. part_o / part_ml hold
 // chunk_cap chunks per (row, kv head); err is the device error word; sched the
 // four chunk counters (zero at launch, reset by the combine). Exactly one of
-// `gated` (final gated bf16 output) and win_o / win_ml (window partials) is
-// used. Returns a LISA_* status.
+// `gated` (final gated bf16 output), win_o / win_ml (window partials) and
+// `xchg` (window partials published to every rank of an exchange) is used.
+// Returns a LISA_* status.
 int run_decode(uint16_t* kc, uint16_t* vc, uint32_t window_rows, uint32_t kv_lo, uint32_t base, int rows,
                int in_dtype, const void* q_gate, const void* k, const void* v, const uint16_t* qn,
                const uint16_t* kn, float eps, float* part_o, float* part_ml, uint32_t chunk_cap, int* err,
-               uint32_t* sched, uint16_t* gated, float* win_o, float* win_ml, int num_sms, cudaStream_t stream);
+               uint32_t* sched, uint16_t* gated, float* win_o, float* win_ml, int num_sms, cudaStream_t stream,
+               const XchgDev* xchg = nullptr);
 
 // Number of SMs of the current device (queried once per device).
 int current_device_sms();

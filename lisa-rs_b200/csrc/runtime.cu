@@ -125,7 +125,8 @@ int current_device_sms() {
 int run_decode(uint16_t* kc, uint16_t* vc, uint32_t window_rows, uint32_t kv_lo, uint32_t base, int rows,
                int in_dtype, const void* q_gate, const void* k, const void* v, const uint16_t* qn,
                const uint16_t* kn, float eps, float* part_o, float* part_ml, uint32_t chunk_cap, int* err,
-               uint32_t* sched, uint16_t* gated, float* win_o, float* win_ml, int num_sms, cudaStream_t stream) {
+               uint32_t* sched, uint16_t* gated, float* win_o, float* win_ml, int num_sms, cudaStream_t stream,
+               const XchgDev* xchg) {
   DecodeParams p = {};
   p.q_gate = q_gate;
   p.k_in = k;
@@ -153,6 +154,7 @@ int run_decode(uint16_t* kc, uint16_t* vc, uint32_t window_rows, uint32_t kv_lo,
   p.gated_out = gated;
   p.win_o = win_o;
   p.win_ml = win_ml;
+  p.xchg = xchg;
   if (p.nchunks > chunk_cap) return LISA_EINVAL;
   // the kernel bulk-copies q rows and the q gains: 16-byte alignment required
   if (((uintptr_t)q_gate & 15) || ((uintptr_t)qn & 15)) return LISA_EINVAL;

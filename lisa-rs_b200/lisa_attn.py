@@ -27,6 +27,7 @@ PREFILL_MAX_ROWS = 512
 
 OK, EINVAL, ENOSPC, ESTATE, ETIMEOUT, ECUDA, E2BIG = 0, -22, -28, -71, -62, -1000, -7
 NOALLOC_MAX_POSITIONS = 16384
+XCHG_HANDLE_BYTES = 64
 DTYPE_F32, DTYPE_BF16 = 0, 1
 _NAMES = {E2BIG: "E2BIG", EINVAL: "EINVAL", ENOSPC: "ENOSPC", ESTATE: "ESTATE", ETIMEOUT: "ETIMEOUT", ECUDA: "ECUDA"}
 
@@ -56,6 +57,12 @@ SIGNATURES = {
                                        _P, _sz, _P]),
     "lisa_attn_merge_windows": (_i32, [_i32, _i32, _P, _P, _i32, _P, _P, _P]),
     "lisa_attn_window_check_device_error": (_i32, [_P, _P]),
+    "lisa_attn_xchg_create": (_i32, [_i32, _i32, _i32, _i32, _u32, ctypes.POINTER(_P)]),
+    "lisa_attn_xchg_handle": (_i32, [_P, _P]),
+    "lisa_attn_xchg_open": (_i32, [_P, _P]),
+    "lisa_attn_xchg_decode": (_i32, [_P, _P, _P, _u32, _u32, _i32, _i32, _P, _P, _P, _P, _P, _f32, _P, _P]),
+    "lisa_attn_xchg_check_device_error": (_i32, [_P, _P]),
+    "lisa_attn_xchg_destroy": (_i32, [_P]),
     "lisa_attn_decode_noalloc": (_i32, [_P, _P, _u32, _u32, _i32, _i32, _P, _P, _P, _P, _P, _f32, _P, _P]),
     "lisa_attn_noalloc_check_device_error": (_i32, []),
     "lisa_attn_debug_wait_fault": (_i32, [_u32, _i32]),
@@ -298,3 +305,53 @@ def merge_windows(n_parts, rows, part_o, part_ml, q_gate, out, stream=None):
     _check("lisa_attn_merge_windows",
            lib.lisa_attn_merge_windows(n_parts, rows, _ptr(part_o), _ptr(part_ml), _dtype_code(q_gate),
                                        _ptr(q_gate), _ptr(out), _stream_ptr(stream)))
+
+
+class WindowExchange:
+    """This rank's end of a split-KV exchange (lisa_attn_xchg_*): a receive
+    region in device memory that every rank of the sequence writes its window
+    partials into. Construct on every rank, all-gather ``handle()`` bytes in
+    rank order with any host transport, then ``open(handles)``."""
+
+    def __init__(self, world: int, rank: int, window_rows: int, max_rows: int = 3, device: int | None = None):
+        import torch
+
+        self.lib = load_library()
+        self.device = torch.cuda.current_device() if device is None else device
+        h = _P()
+        _check("lisa_attn_xchg_create",
+               self.lib.lisa_attn_xchg_create(self.device, world, rank, max_rows, window_rows, ctypes.byref(h)))
+        self._h = h
+        self.world, self.rank, self.max_rows = world, rank, max_rows
+
+    def handle(self) -> bytes:
+        buf = ctypes.create_string_buffer(XCHG_HANDLE_BYTES)
+        _check("lisa_attn_xchg_handle", self.lib.lisa_attn_xchg_handle(self._h, buf))
+        return buf.raw
+
+    def open(self, handles: list[bytes]) -> None:
+        assert len(handles) == self.world and all(len(b) == XCHG_HANDLE_BYTES for b in handles)
+        blob = ctypes.create_string_buffer(b"".join(handles), XCHG_HANDLE_BYTES * self.world)
+        _check("lisa_attn_xchg_open", self.lib.lisa_attn_xchg_open(self._h, blob))
+
+    def decode(self, k_cache, v_cache, kv_lo, base, rows, q_gate, k, v, w, out, eps=1e-6, stream=None):
+        _check("lisa_attn_xchg_decode",
+               self.lib.lisa_attn_xchg_decode(self._h, _ptr(k_cache), _ptr(v_cache), kv_lo, base, rows,
+                                              _dtype_code(q_gate), _ptr(q_gate), _ptr(k), _ptr(v), _ptr(w.q_norm),
+                                              _ptr(w.k_norm), eps, _ptr(out), _stream_ptr(stream)))
+        return out
+
+    def check_device_error(self, stream=None) -> None:
+        _check("lisa_attn_xchg_check_device_error",
+               self.lib.lisa_attn_xchg_check_device_error(self._h, _stream_ptr(stream)))
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            self.lib.lisa_attn_xchg_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

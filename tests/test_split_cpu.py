@@ -102,3 +102,72 @@ def test_gather_and_merge_over_gloo_world2(tmp_path):
     merged = np.load(out)
     want = O.sdpa(query, kc, vc, base, sliced=False)
     assert np.abs(merged - want).max() < 1e-4
+
+
+def _monitor_rank(rank, world, port, mode, result_path):
+    import datetime
+    import json
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+    store = dist.TCPStore("127.0.0.1", port + 1, world, rank == 0, timeout=datetime.timedelta(seconds=10))
+    mon = lisa_split.PeerMonitor(store, rank, world, interval=0.05, stale_after=1.0)
+    po = torch.full((1, QH, HD), float(rank))
+    pm = torch.zeros((1, QH, 2))
+    for _ in range(3):  # steps with every rank present
+        mon.check()
+        all_o, _ = lisa_split.gather_partials(po, pm)
+        assert all_o.shape[0] == world
+    dist.barrier()
+    if rank == 1:
+        if mode == "leave":
+            mon.leave()
+        os._exit(0)  # between steps: nothing of this rank is in flight
+    # rank 0 goes on stepping: the check before the launch must stop it
+    t0 = time.monotonic()
+    res = {"raised": False}
+    while time.monotonic() - t0 < 10.0:
+        try:
+            mon.check()
+        except lisa_split.PeerLost as e:
+            res = {"raised": True, "why": str(e), "after_s": time.monotonic() - t0}
+            break
+        time.sleep(0.02)
+    # a collective issued anyway ends with an error instead of hanging
+    t1 = time.monotonic()
+    try:
+        lisa_split.gather_partials(po, pm)
+        res["collective"] = "returned"
+    except Exception as e:
+        res["collective"] = type(e).__name__
+    res["collective_s"] = time.monotonic() - t1
+    with open(result_path, "w") as f:
+        json.dump(res, f)
+    os._exit(0)
+
+
+@pytest.mark.parametrize("mode", ["leave", "vanish"])
+def test_rank_departure_between_steps_is_reported_not_hung(mode, tmp_path):
+    """SplitKVDecoder's host-side failure detection on gloo CPU ranks: rank 1
+    leaves between steps (announced, or silently); rank 0's next pre-launch
+    check raises PeerLost within seconds, and a collective issued anyway
+    fails (process-group timeout or closed peer) instead of hanging."""
+    import json
+    import socket
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    out = str(tmp_path / "res.json")
+    mp.spawn(_monitor_rank, args=(2, port, mode, out), nprocs=2, join=True)
+    res = json.load(open(out))
+    assert res["raised"], res
+    assert res["after_s"] < 5.0, res
+    assert res["collective"] != "returned" and res["collective_s"] < 30.0, res

@@ -110,3 +110,115 @@ def test_window_argument_errors():
     bad[15] = ws.data_ptr() + 8  # misaligned workspace
     assert lib.lisa_attn_decode_window(*bad) == lisa_attn.EINVAL
     torch.cuda.synchronize()
+
+
+def _exchange_case(rng, base, rows):
+    qn, kn = norm_weights(rng)
+    q, k, v = layer_inputs(rng, rows)
+    kc = torch.randn((KVH, base + rows, HD), device="cuda").to(torch.bfloat16)
+    vc = torch.randn((KVH, base + rows, HD), device="cuda").to(torch.bfloat16)
+    kc[:, base:] = 0
+    vc[:, base:] = 0
+    return qn, kn, q, k, v, kc, vc
+
+
+@pytest.mark.parametrize("rows", [1, 3])
+def test_exchange_world1_matches_context_and_replays_in_a_graph(rows):
+    """lisa_attn_xchg_decode with one rank: the split, the publishing combine
+    and the bounded-wait merge against the single-context decode; then the
+    same step captured in a CUDA graph and replayed several times (the step
+    counter lives on the device), every replay equal to the eager result."""
+    rng = np.random.default_rng(800 + rows)
+    base = 5000
+    qn, kn, q, k, v, kc, vc = _exchange_case(rng, base, rows)
+    w = weights(qn, kn)
+    dec = lisa_split.SplitKVDecoder(lisa_split.Window(0, 0, base + rows), max_rows=3)
+    dec.k.copy_(kc)
+    dec.v.copy_(vc)
+    tq, tk, tv = dev_inputs(q, k, v)
+    got = to_bits(dec.decode(base, tq, tk, tv, w))
+    dec.check_device_error()
+    r = lisa_attn.AttnRunner(1, base + rows)
+    rk, rv = r.kv_cache(0)
+    rk.copy_(kc)
+    rv.copy_(vc)
+    want = to_bits(r.decode_layer(0, base, rows, tq, tk, tv, w))
+    assert_close_bf16(got, want, f"exchange world=1 rows={rows}")
+    assert torch.equal(dec.k, rk) and torch.equal(dec.v, rv)
+    out = torch.empty((rows, OROW), dtype=torch.bfloat16, device="cuda")
+    s = torch.cuda.Stream()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        dec.decode(base, tq, tk, tv, w, out, stream=s)  # warm-up on the capture stream
+        s.synchronize()
+        with torch.cuda.graph(g, stream=s):
+            dec.decode(base, tq, tk, tv, w, out, stream=s)
+    for _ in range(5):
+        out.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        assert np.array_equal(to_bits(out), got)
+    dec.check_device_error()
+
+
+def _exchange_rank(rank, world, port, base, rows, seed, result_dir):
+    import os
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    rng = np.random.default_rng(seed)
+    qn, kn = norm_weights(rng)
+    q, k, v = layer_inputs(rng, rows)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    kc = torch.randn((KVH, base + rows, HD), device="cuda", generator=g).to(torch.bfloat16)
+    vc = torch.randn((KVH, base + rows, HD), device="cuda", generator=g).to(torch.bfloat16)
+    kc[:, base:] = 0
+    vc[:, base:] = 0
+    win = lisa_split.plan_windows(base + rows, world)[rank]
+    dec = lisa_split.SplitKVDecoder(win, max_rows=3)
+    if win.rows:
+        dec.k[:, :win.rows].copy_(kc[:, win.lo:win.lo + win.rows])
+        dec.v[:, :win.rows].copy_(vc[:, win.lo:win.lo + win.rows])
+    w = weights(qn, kn)
+    tq, tk, tv = dev_inputs(q, k, v)
+    outs = []
+    for _ in range(3):  # several steps: both receive parities and the flags' step numbers
+        outs.append(to_bits(dec.decode(base, tq, tk, tv, w)))
+    dec.check_device_error()
+    np.save(os.path.join(result_dir, f"rank{rank}.npy"), np.stack(outs))
+    if rank == 0:
+        r = lisa_attn.AttnRunner(1, base + rows)
+        rk, rv = r.kv_cache(0)
+        rk.copy_(kc)
+        rv.copy_(vc)
+        np.save(os.path.join(result_dir, "single.npy"), to_bits(r.decode_layer(0, base, rows, tq, tk, tv, w)))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 or more GPUs")
+@pytest.mark.parametrize("rows", [1, 3])
+def test_exchange_across_gpus(rows, tmp_path):
+    """Config 4's exchange on real GPUs (one process per GPU, peer stores over
+    NVLink, no NVLS): every rank's gated output equals the single-GPU
+    context decode of the whole sequence, on three consecutive steps."""
+    import socket
+
+    import torch.multiprocessing as mp
+
+    world = min(torch.cuda.device_count(), 8)
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    base = 20000
+    mp.spawn(_exchange_rank, args=(world, port, base, rows, 4242 + rows, str(tmp_path)), nprocs=world, join=True)
+    single = np.load(tmp_path / "single.npy")
+    for rank in range(world):
+        outs = np.load(tmp_path / f"rank{rank}.npy")
+        for o in outs:
+            assert_close_bf16(o, single, f"rank {rank}")
+        assert np.array_equal(outs[0], np.load(tmp_path / "rank0.npy")[0])  # every rank: identical bits
