@@ -442,8 +442,10 @@ def bench_longctx(args, rank, world, local, rows=1):
 def bench_batched(args, rank, world, local):
     """64 sequences, contexts U[1024, 32768] (seeded), 16
     attention layers each, M=1; sequences sharded over ranks (lisa_split
-    plan_sequences), no collective. value = µs per layer step (all 64
-    sequences through one layer)."""
+    plan_sequences), no collective. Per layer, this rank's sequences go
+    through one lisa_attn_decode_batch call (3 launches); the 16 layer calls
+    of a step are one CUDA graph. value = µs per layer step (all 64 sequences
+    through one layer)."""
     import numpy as np
     import torch
 
@@ -463,39 +465,38 @@ def bench_batched(args, rank, world, local):
             kc, vc = r.kv_cache(layer)
             fill_random(kc, gen)
             fill_random(vc, gen)
-        runners.append((r, ctx[i] - 1))
+        runners.append(r)
+    bases = [ctx[i] - 1 for i in mine]
+    n = len(runners)
+    bd = lisa_attn.BatchDecoder(n, sum(ctx[i] for i in mine))
     ws = make_weights(gen, LAYERS)
-    q = torch.randn((1, QROW), generator=gen, device="cuda")
-    k = torch.randn((1, KROW), generator=gen, device="cuda")
-    v = torch.randn((1, KROW), generator=gen, device="cuda")
-    out = torch.empty((1, OROW), dtype=torch.bfloat16, device="cuda")
+    q = torch.randn((LAYERS, n, QROW), generator=gen, device="cuda")
+    k = torch.randn((LAYERS, n, KROW), generator=gen, device="cuda")
+    v = torch.randn((LAYERS, n, KROW), generator=gen, device="cuda")
+    out = torch.empty((LAYERS, n, OROW), dtype=torch.bfloat16, device="cuda")
 
-    def step_eager():
+    def step_on(st):
         for layer in range(LAYERS):
-            for r, base in runners:
-                r.decode_layer(layer, base, 1, q, k, v, ws[layer], out, stream)
+            bd.decode(runners, layer, bases, q[layer], k[layer], v[layer], ws[layer], out[layer], st)
 
-    # One step is ~1000 library calls; replaying it as a CUDA graph removes the
-    # Python call overhead from the measurement (the kernels are the same).
-    step_eager()
+    step_on(stream)
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
     cap_stream = torch.cuda.Stream()
     with torch.cuda.stream(cap_stream):
         with torch.cuda.graph(graph, stream=cap_stream):
-            for layer in range(LAYERS):
-                for r, base in runners:
-                    r.decode_layer(layer, base, 1, q, k, v, ws[layer], out, cap_stream)
+            step_on(cap_stream)
     torch.cuda.synchronize()
 
-    def step():
-        graph.replay()
-
     with ClockSampler(local) as clk:
-        ms = timed(step, args.steps, args.warmup, world, stream)
+        for _ in range(10):
+            graph.replay()
+        torch.cuda.synchronize()
+        ms = timed(graph.replay, args.steps, args.warmup, world, stream)
+    bd.check_device_error()
     total_ctx = sum(ctx)
     return {"ms": ms, "clocks": clk.summary(), "bytes": 4096 * total_ctx * LAYERS, "ctx_sum": total_ctx,
-            "launches": 2 * LAYERS * len(runners)}
+            "launches": 3 * LAYERS}
 
 
 def emit(line: dict) -> None:

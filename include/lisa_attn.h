@@ -189,6 +189,33 @@ int lisa_attn_window_check_device_error(void* workspace, void* stream);
 int lisa_attn_merge_windows(int n_parts, int rows, const float* part_o, const float* part_ml,
                             int in_dtype, const void* q_gate, uint16_t* gated_out, void* stream);
 
+/* ---- batched decode of many sequences -------------------------------------
+ * One M=1 decode step of one attention layer for n_seqs independent
+ * sequences, each with its own context (KV cache, capacity), in three kernel
+ * launches: encode_attention (runner.rs:1426-1592) for batch 1, taken over all
+ * sequences at once. Row i of q_gate [n_seqs][24][512], k, v [n_seqs][4][256]
+ * and gated_out [n_seqs][6144] belongs to ctxs[i], whose new row is appended
+ * at bases[i] (host array); sequence i attends positions 0..bases[i]. The
+ * norm gains are shared (one model). Positions are not advanced (call
+ * lisa_attn_advance per context, as after lisa_attn_decode). Results equal
+ * lisa_attn_decode's for each sequence within the decode tolerance.
+ * A lisa_attn_batch owns the scratch for up to max_seqs sequences
+ * (<= LISA_ATTN_BATCH_MAX_SEQS) whose contexts sum to at most
+ * max_total_positions (LISA_E2BIG beyond). Every context must live on the
+ * batch's device (LISA_EINVAL); bases[i] + 1 > capacity gives LISA_ENOSPC.
+ * Calls on one batch object must not overlap on the GPU. */
+#define LISA_ATTN_BATCH_MAX_SEQS 128
+typedef struct lisa_attn_batch lisa_attn_batch;
+int lisa_attn_batch_create(int device, int max_seqs, uint64_t max_total_positions, lisa_attn_batch** out);
+int lisa_attn_batch_destroy(lisa_attn_batch* b);
+int lisa_attn_decode_batch(lisa_attn_batch* b, int n_seqs, lisa_attn_ctx* const* ctxs, int layer,
+                           const uint32_t* bases, int in_dtype, const void* q_gate, const void* k, const void* v,
+                           const uint16_t* q_norm_w, const uint16_t* k_norm_w, float eps, uint16_t* gated_out,
+                           void* stream);
+/* Synchronises `stream`; LISA_ETIMEOUT if a bounded wait of an earlier
+ * lisa_attn_decode_batch call gave up (its output is not valid); clears. */
+int lisa_attn_batch_check_device_error(lisa_attn_batch* b, void* stream);
+
 /* ---- split-KV decode with a peer-memory exchange (multi-GPU) ---------------
  * No lisa-rs counterpart (lisa-rs drives one GPU). One long sequence's KV is
  * split into contiguous windows, one per rank (one process per GPU, the GPUs

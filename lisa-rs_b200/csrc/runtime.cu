@@ -22,27 +22,10 @@
 #include "prefill.cuh"
 #include "common.cuh"
 #include "dispatch.h"
+#include "ctx.h"
 
 using namespace lisa;
 
-struct lisa_attn_ctx {
-  int device = 0;
-  int n_layers = 0;
-  uint32_t capacity = 0;
-  uint16_t* k = nullptr;  // [layer][4][capacity][256]
-  uint16_t* v = nullptr;
-  float* part_o = nullptr;   // decode chunk partials
-  float* part_ml = nullptr;
-  uint32_t chunk_cap = 0;
-  void* prefill_ws = nullptr;  // prefill scratch
-  size_t prefill_ws_bytes = 0;
-  int* err = nullptr;
-  uint32_t* sched = nullptr;  // decode chunk counters [4]
-  int num_sms = 148;
-  uint32_t position = 0;
-  bool verify_pending = false;
-  uint32_t verify_base = 0;
-};
 
 namespace {
 
@@ -223,6 +206,21 @@ int lisa_attn_create(int device, int n_layers, uint32_t capacity, lisa_attn_ctx*
   ok = ok && cudaMemset(c->k, 0, cache_bytes) == cudaSuccess && cudaMemset(c->v, 0, cache_bytes) == cudaSuccess &&
        cudaMemset(c->err, 0, sizeof(int)) == cudaSuccess && cudaMemset(c->sched, 0, 64) == cudaSuccess &&
        cudaDeviceSynchronize() == cudaSuccess;
+  // Tensor maps of every layer's K and V over the whole capacity (64-position
+  // boxes of all four dim groups), kept on the device for the batched decode,
+  // whose sequences each bring their own maps.
+  ok = ok && cudaMalloc(&c->tmaps, (size_t)n_layers * 2 * sizeof(CUtensorMap)) == cudaSuccess;
+  if (ok) {
+    CUtensorMap* h = new CUtensorMap[(size_t)n_layers * 2];
+    for (int l = 0; ok && l < n_layers; ++l) {
+      const size_t off = (size_t)l * layer_elems(c);
+      ok = lisa_encode_group_map(&h[2 * l], c->k + off, capacity, capacity, KVH, DEC_TILE, 4) == LISA_OK &&
+           lisa_encode_group_map(&h[2 * l + 1], c->v + off, capacity, capacity, KVH, DEC_TILE, 4) == LISA_OK;
+    }
+    ok = ok && cudaMemcpy(c->tmaps, h, (size_t)n_layers * 2 * sizeof(CUtensorMap), cudaMemcpyHostToDevice) ==
+                   cudaSuccess;
+    delete[] h;
+  }
   if (!ok) {
     lisa_attn_destroy(c);
     return LISA_ECUDA;
@@ -241,6 +239,7 @@ int lisa_attn_destroy(lisa_attn_ctx* c) {
   cudaFree(c->prefill_ws);
   cudaFree(c->err);
   cudaFree(c->sched);
+  cudaFree(c->tmaps);
   delete c;
   return LISA_OK;
 }

@@ -28,6 +28,7 @@ PREFILL_MAX_ROWS = 512
 OK, EINVAL, ENOSPC, ESTATE, ETIMEOUT, ECUDA, E2BIG = 0, -22, -28, -71, -62, -1000, -7
 NOALLOC_MAX_POSITIONS = 16384
 XCHG_HANDLE_BYTES = 64
+BATCH_MAX_SEQS = 128
 DTYPE_F32, DTYPE_BF16 = 0, 1
 _NAMES = {E2BIG: "E2BIG", EINVAL: "EINVAL", ENOSPC: "ENOSPC", ESTATE: "ESTATE", ETIMEOUT: "ETIMEOUT", ECUDA: "ECUDA"}
 
@@ -57,6 +58,10 @@ SIGNATURES = {
                                        _P, _sz, _P]),
     "lisa_attn_merge_windows": (_i32, [_i32, _i32, _P, _P, _i32, _P, _P, _P]),
     "lisa_attn_window_check_device_error": (_i32, [_P, _P]),
+    "lisa_attn_batch_create": (_i32, [_i32, _i32, ctypes.c_uint64, ctypes.POINTER(_P)]),
+    "lisa_attn_batch_destroy": (_i32, [_P]),
+    "lisa_attn_decode_batch": (_i32, [_P, _i32, _P, _i32, _P, _i32, _P, _P, _P, _P, _P, _f32, _P, _P]),
+    "lisa_attn_batch_check_device_error": (_i32, [_P, _P]),
     "lisa_attn_xchg_create": (_i32, [_i32, _i32, _i32, _i32, _u32, ctypes.POINTER(_P)]),
     "lisa_attn_xchg_handle": (_i32, [_P, _P]),
     "lisa_attn_xchg_open": (_i32, [_P, _P]),
@@ -348,6 +353,58 @@ class WindowExchange:
     def close(self) -> None:
         if getattr(self, "_h", None):
             self.lib.lisa_attn_xchg_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class BatchDecoder:
+    """lisa_attn_decode_batch: one M=1 decode step of one layer for many
+    sequences (each an AttnRunner with its own KV cache) in three launches.
+    Scratch for up to ``max_seqs`` sequences whose capacities sum to at most
+    ``max_total_positions``."""
+
+    def __init__(self, max_seqs: int, max_total_positions: int, device: int | None = None, eps: float = 1e-6):
+        import torch
+
+        self.lib = load_library()
+        self.device = torch.cuda.current_device() if device is None else device
+        self.eps = eps
+        h = _P()
+        _check("lisa_attn_batch_create",
+               self.lib.lisa_attn_batch_create(self.device, max_seqs, max_total_positions, ctypes.byref(h)))
+        self._h = h
+        self._keep = None
+
+    def decode(self, runners, layer, bases, q_gate, k, v, w, out=None, stream=None):
+        """q_gate [n, 12288], k, v [n, 1024] (f32 or bf16), row i for
+        runners[i] at position bases[i]; returns gated bf16 [n, 6144]."""
+        import torch
+
+        n = len(runners)
+        assert len(bases) == n and q_gate.numel() == n * QROW and k.numel() == n * KROW and v.numel() == n * KROW
+        if out is None:
+            out = torch.empty((n, OROW), dtype=torch.bfloat16, device=q_gate.device)
+        ctxs = (_P * n)(*[r.handle.value for r in runners])
+        bs = (_u32 * n)(*bases)
+        self._keep = (ctxs, bs)
+        _check("lisa_attn_decode_batch",
+               self.lib.lisa_attn_decode_batch(self._h, n, ctxs, layer, bs, _dtype_code(q_gate), _ptr(q_gate),
+                                               _ptr(k), _ptr(v), _ptr(w.q_norm), _ptr(w.k_norm), self.eps,
+                                               _ptr(out), _stream_ptr(stream)))
+        return out
+
+    def check_device_error(self, stream=None) -> None:
+        _check("lisa_attn_batch_check_device_error",
+               self.lib.lisa_attn_batch_check_device_error(self._h, _stream_ptr(stream)))
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            self.lib.lisa_attn_batch_destroy(self._h)
             self._h = None
 
     def __del__(self):

@@ -104,3 +104,27 @@ def test_contexts_on_two_devices_in_one_process():
             r.check_device_error()
             outs.append((a, b))
     assert np.array_equal(outs[0][0], outs[1][0]) and np.array_equal(outs[0][1], outs[1][1])
+
+
+def test_batch_decode_reports_timeout_then_recovers():
+    rng = np.random.default_rng(970)
+    qn, kn = norm_weights(rng)
+    w = weights(qn, kn)
+    runs = [lisa_attn.AttnRunner(1, 3000) for _ in range(3)]
+    bases = [100, 2000, 2999]
+    for r, b in zip(runs, bases):
+        kc, vc = random_cache(rng, 3000, b)
+        load_cache(r, 0, kc, vc)
+    q, k, v = layer_inputs(rng, 3)
+    tq, tk, tv = dev_inputs(q, k, v)
+    bd = lisa_attn.BatchDecoder(3, 9000)
+    with injected_timeout():
+        bd.decode(runs, 0, bases, tq, tk, tv, w)
+        with pytest.raises(lisa_attn.LisaError) as e:
+            bd.check_device_error()
+        assert e.value.status == lisa_attn.ETIMEOUT
+    got = to_bits(bd.decode(runs, 0, bases, tq, tk, tv, w))
+    bd.check_device_error()
+    for i, r in enumerate(runs):
+        ref = to_bits(r.decode_layer(0, bases[i], 1, tq[i:i + 1], tk[i:i + 1], tv[i:i + 1], w))
+        assert_close_bf16(got[i:i + 1], ref, f"seq {i}")
