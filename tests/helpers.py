@@ -63,18 +63,29 @@ def argmax_projection(gated_bits: np.ndarray, seed: int = 1234, n_out: int = 102
     return np.argmax(projection_logits(gated_bits, seed, n_out), axis=1)
 
 
-def assert_argmax_agrees(got_bits: np.ndarray, want_bits: np.ndarray, what: str = "") -> int:
-    """The north star's exact-argmax check on a synthetic projection. A row may
-    only disagree where the oracle's own top two logits are closer than the
-    logit perturbation the two outputs differ by (a tie at the output
-    tolerance); returns the number of such tie rows."""
+FLIP_LOG: list[dict] = []  # every argmax disagreement seen in this process (what, row, gap, perturbation)
+
+
+def assert_argmax_agrees(got_bits: np.ndarray, want_bits: np.ndarray, what: str = "", exact: bool = True) -> int:
+    """The north star's exact-argmax check on a synthetic projection of every
+    row. exact=True (every BASELINE config): no row may disagree. exact=False
+    (off-config edge cases): a row may only disagree where the oracle's own
+    top two logits are closer than twice the logit perturbation between the
+    two outputs (a tie at the output tolerance), at most 1 % of rows. Every
+    disagreement is logged in FLIP_LOG and printed with its gap; returns the
+    number of disagreeing rows."""
     lg, lw = projection_logits(got_bits), projection_logits(want_bits)
     ag, aw = lg.argmax(1), lw.argmax(1)
     diff = ag != aw
-    if not diff.any():
-        return 0
     rows = np.nonzero(diff)[0]
     pert = np.abs(lg - lw).max(1)
+    for r in rows:
+        rec = {"what": what, "row": int(r), "gap": float(lw[r, aw[r]] - lw[r, ag[r]]), "perturbation": float(pert[r])}
+        FLIP_LOG.append(rec)
+        print(f"argmax flip: {rec}")
+    if exact:
+        assert not diff.any(), f"{what}: argmax differs in {diff.sum()} of {diff.size} rows: {FLIP_LOG[-len(rows):]}"
+        return 0
     gap = lw[rows, aw[rows]] - lw[rows, ag[rows]]
     bad = gap > 2 * pert[rows]
     assert not bad.any(), f"{what}: argmax differs beyond ties in rows {rows[bad][:10]}"

@@ -61,7 +61,48 @@ def test_verify_m3(base):
     """BASELINE config 1 (base 8189) and chunk-boundary straddles."""
     got, want, *_ = run_case(200 + base, base + 3, base, 3)
     assert_close_bf16(got, want, f"verify base={base}")
-    assert_argmax_agrees(got, want, "argmax")
+    assert_argmax_agrees(got, want, f"verify base={base}")
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2, 3, 4, 5])
+def test_config1_verify_trim_rerun(seed):
+    """BASELINE config 1 as written: M=3 verify at positions 8189..8191 over an
+    8189-token cache; then the KV is trimmed to a seeded accepted prefix of 1,
+    2 or 3 rows (commit_verified_prefix) and the verify re-runs at the new
+    position; both verifies against the oracle, whose cache received only the
+    accepted rows of the first."""
+    rng = np.random.default_rng(0x5EED + 1 + 100 * seed)
+    accepted = int(rng.integers(1, 4))
+    base = 8189
+    cap = base + 6
+    qn, kn = norm_weights(rng)
+    w = weights(qn, kn)
+    kc, vc = random_cache(rng, cap, base)
+    r = lisa_attn.AttnRunner(1, cap)
+    load_cache(r, 0, kc, vc)
+    r.restore_position(base)
+    qa, ka, va = layer_inputs(rng, 3)
+    got_a = to_bits(r.verify_block3(0, *dev_inputs(qa, ka, va), w))
+    r.advance(3, verify=True)
+    kco, vco = kc.copy(), vc.copy()
+    want_a = O.attention_layer(qa, ka, va, base, qn, kn, kco, vco, sliced=True)
+    assert_close_bf16(got_a, want_a, "config 1 first verify")
+    assert_argmax_agrees(got_a, want_a, "config 1 first verify")
+    r.commit_verified_prefix(accepted)
+    assert r.position() == base + accepted
+    # the oracle's cache holds only the accepted rows (rejected rows are
+    # overwritten by the re-run, as in runner.rs:911-944)
+    kco, vco = kc.copy(), vc.copy()
+    O.attention_layer(qa[:accepted], ka[:accepted], va[:accepted], base, qn, kn, kco, vco, sliced=True)
+    qb, kb, vb = layer_inputs(rng, 3)
+    got_b = to_bits(r.verify_block3(0, *dev_inputs(qb, kb, vb), w))
+    r.advance(3, verify=True)
+    r.check_device_error()
+    want_b = O.attention_layer(qb, kb, vb, base + accepted, qn, kn, kco, vco, sliced=True)
+    assert_close_bf16(got_b, want_b, f"config 1 re-run after accepting {accepted}")
+    assert_argmax_agrees(got_b, want_b, f"config 1 re-run after accepting {accepted}")
+    gk, gv = read_cache(r, 0)
+    assert np.array_equal(gv[:, :base + accepted + 3], vco[:, :base + accepted + 3])
 
 
 @pytest.mark.parametrize("base", [3, 126, 127, 128, 1000, 8189])

@@ -3,13 +3,14 @@ import numpy as np
 import pytest
 
 import oracle as O
-from helpers import HD, KROW, OROW, QROW, assert_close_bf16, assert_argmax_agrees, layer_inputs, norm_weights
+from helpers import (HD, KROW, OROW, QROW, assert_argmax_agrees, assert_close_bf16, layer_inputs, norm_weights,
+                     random_cache)
 
 pytestmark = pytest.mark.gpu
 
 torch = pytest.importorskip("torch")
 import lisa_attn  # noqa: E402
-from gpu_util import dev_inputs, read_cache, to_bits, weights  # noqa: E402
+from gpu_util import dev_inputs, load_cache, read_cache, to_bits, weights  # noqa: E402
 
 
 def gpu_prefill(q, k, v, qn, kn, chunks, capacity, dtype=torch.float32):
@@ -58,7 +59,7 @@ def test_prefill_matches_oracle(chunks):
         pos += m
     want = np.concatenate(want)
     assert_close_bf16(got, want, f"prefill {chunks}")
-    assert_argmax_agrees(got, want, "argmax")
+    assert_argmax_agrees(got, want, f"prefill {chunks}", exact=False)
     gk, gv = read_cache(r, 0)
     assert np.array_equal(gv[:, :n], vc[:, :n])
     kd = np.abs(O.bf16_to_f32(gk[:, :n]) - O.bf16_to_f32(kc[:, :n]))
@@ -67,16 +68,52 @@ def test_prefill_matches_oracle(chunks):
 
 def test_config2_prefill_4096_in_512_chunks():
     """BASELINE config 2: 4096 tokens from an empty cache, 8 chunks of 512;
-    sampled rows of every chunk against the oracle."""
+    every one of the 4096 rows against the oracle, and the whole cache."""
     n = 4096
     rng = np.random.default_rng(0x5EED + 2)
     qn, kn = norm_weights(rng)
     q, k, v = layer_inputs(rng, n)
     got, r = gpu_prefill(q, k, v, qn, kn, [512] * 8, n)
-    sample = sorted({0, 1, 63, 64, 127, 128, 511, 512, 1000, 2047, 2048, 3071, 3584, 4000, 4094, 4095})
-    want, kc, vc = oracle_rows(q, k, v, qn, kn, n, sample)
-    for row in sample:
-        assert_close_bf16(got[row], want[row], f"row {row}")
+    kc = np.zeros((4, n, HD), np.uint16)
+    vc = np.zeros((4, n, HD), np.uint16)
+    want = np.concatenate([O.attention_layer(q[b:b + 512], k[b:b + 512], v[b:b + 512], b, qn, kn, kc, vc,
+                                             sliced=False) for b in range(0, n, 512)])
+    assert_close_bf16(got, want, "config 2, all rows")
+    flips = assert_argmax_agrees(got, want, "config 2", exact=False)
+    print(f"config 2: {flips} argmax tie flips over {n} rows")
+    gk, gv = read_cache(r, 0)
+    assert np.array_equal(gv, vc)
+    kd = np.abs(O.bf16_to_f32(gk) - O.bf16_to_f32(kc))
+    assert kd.max() <= 2 ** -7 * np.abs(O.bf16_to_f32(kc)).max()
+
+
+def test_prefill_chunk_at_32k_then_decode_at_last_position():
+    """A 512-row chunk at base 32256 of a 32768-capacity context over a
+    filled cache (key tiles up to 256 deep, TMA coordinates near the top of
+    the cache), all rows against the oracle; then the last position is
+    trimmed and decoded again (M=1 at 32767) over what the prefill wrote."""
+    cap, base, m = 32768, 32256, 512
+    rng = np.random.default_rng(0x5EED + 32)
+    qn, kn = norm_weights(rng)
+    w = weights(qn, kn)
+    kc, vc = random_cache(rng, cap, base)
+    r = lisa_attn.AttnRunner(1, cap)
+    load_cache(r, 0, kc, vc)
+    r.restore_position(base)
+    q, k, v = layer_inputs(rng, m)
+    got = to_bits(r.forward_prefill(0, *dev_inputs(q, k, v), w))
+    r.advance(m)
+    want = O.attention_layer(q, k, v, base, qn, kn, kc, vc, sliced=False)
+    assert_close_bf16(got, want, "chunk at 32256")
+    assert_argmax_agrees(got, want, "chunk at 32256", exact=False)
+    r.trim_state(1)
+    assert r.position() == cap - 1
+    q1, k1, v1 = layer_inputs(rng, 1)
+    got1 = to_bits(r.forward_decode(0, *dev_inputs(q1, k1, v1), w))
+    r.check_device_error()
+    want1 = O.attention_layer(q1, k1, v1, cap - 1, qn, kn, kc, vc, sliced=True)
+    assert_close_bf16(got1, want1, "decode at 32767")
+    assert_argmax_agrees(got1, want1, "decode at 32767")
 
 
 def test_prefill_then_decode_continues():
