@@ -295,6 +295,40 @@ int lisa_attn_noalloc_check_device_error(void);
  * withhold_loads without a limit or a limit above 10 s. */
 int lisa_attn_debug_wait_fault(uint32_t wait_limit_us, int withhold_loads);
 
+/* ---- device bridge ----------------------------------------------------------
+ * Thin wrappers over the CUDA runtime so a host in another language drives the
+ * entry points above with this library alone. They replace lisa-rs's Metal
+ * bridge (src/device/metal.rs): MetalDevice::name / max_working_set (160-175)
+ * -> lisa_attn_dev_info; new_buffer (176-199) and Drop (414-420) ->
+ * lisa_attn_buffer_alloc / _free; new_command_queue (200-206) ->
+ * lisa_attn_stream_create; commit + wait_until_completed (314-321) ->
+ * lisa_attn_stream_synchronize; MetalBuffer::write_bytes / read_bytes
+ * (396-410) -> lisa_attn_copy_h2d / _d2h (device memory is not CPU-visible
+ * here, so these are stream-ordered copies; from pinned host memory they are
+ * asynchronous). Events order work across streams and time it. A stream
+ * argument of NULL is the legacy default stream. All return LISA_OK,
+ * LISA_EINVAL (null pointer, bad device) or LISA_ECUDA. */
+int lisa_attn_dev_count(int* count);
+int lisa_attn_dev_info(int device, char* name, size_t name_bytes, uint64_t* total_bytes, int* sm_count);
+int lisa_attn_dev_select(int device);
+int lisa_attn_buffer_alloc(int device, size_t bytes, void** ptr);
+int lisa_attn_buffer_free(void* ptr);
+int lisa_attn_host_alloc(size_t bytes, void** ptr); /* page-locked host memory */
+int lisa_attn_host_free(void* ptr);
+int lisa_attn_stream_create(int device, void** stream);
+int lisa_attn_stream_destroy(void* stream);
+int lisa_attn_stream_synchronize(void* stream);
+int lisa_attn_event_create(int device, int timing, void** event);
+int lisa_attn_event_destroy(void* event);
+int lisa_attn_event_record(void* event, void* stream);
+int lisa_attn_stream_wait_event(void* stream, void* event);
+int lisa_attn_event_synchronize(void* event);
+int lisa_attn_event_elapsed_ms(void* start, void* end, float* ms);
+int lisa_attn_copy_h2d(void* dst, const void* src, size_t bytes, void* stream);
+int lisa_attn_copy_d2h(void* dst, const void* src, size_t bytes, void* stream);
+int lisa_attn_copy_d2d(void* dst, const void* src, size_t bytes, void* stream);
+int lisa_attn_memset(void* dst, int value, size_t bytes, void* stream);
+
 /* Library build identification (for tests: the .so in use). */
 const char* lisa_attn_build_info(void);
 

@@ -71,6 +71,26 @@ SIGNATURES = {
     "lisa_attn_decode_noalloc": (_i32, [_P, _P, _u32, _u32, _i32, _i32, _P, _P, _P, _P, _P, _f32, _P, _P]),
     "lisa_attn_noalloc_check_device_error": (_i32, []),
     "lisa_attn_debug_wait_fault": (_i32, [_u32, _i32]),
+    "lisa_attn_dev_count": (_i32, [ctypes.POINTER(_i32)]),
+    "lisa_attn_dev_info": (_i32, [_i32, ctypes.c_char_p, _sz, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(_i32)]),
+    "lisa_attn_dev_select": (_i32, [_i32]),
+    "lisa_attn_buffer_alloc": (_i32, [_i32, _sz, ctypes.POINTER(_P)]),
+    "lisa_attn_buffer_free": (_i32, [_P]),
+    "lisa_attn_host_alloc": (_i32, [_sz, ctypes.POINTER(_P)]),
+    "lisa_attn_host_free": (_i32, [_P]),
+    "lisa_attn_stream_create": (_i32, [_i32, ctypes.POINTER(_P)]),
+    "lisa_attn_stream_destroy": (_i32, [_P]),
+    "lisa_attn_stream_synchronize": (_i32, [_P]),
+    "lisa_attn_event_create": (_i32, [_i32, _i32, ctypes.POINTER(_P)]),
+    "lisa_attn_event_destroy": (_i32, [_P]),
+    "lisa_attn_event_record": (_i32, [_P, _P]),
+    "lisa_attn_stream_wait_event": (_i32, [_P, _P]),
+    "lisa_attn_event_synchronize": (_i32, [_P]),
+    "lisa_attn_event_elapsed_ms": (_i32, [_P, _P, ctypes.POINTER(_f32)]),
+    "lisa_attn_copy_h2d": (_i32, [_P, _P, _sz, _P]),
+    "lisa_attn_copy_d2h": (_i32, [_P, _P, _sz, _P]),
+    "lisa_attn_copy_d2d": (_i32, [_P, _P, _sz, _P]),
+    "lisa_attn_memset": (_i32, [_P, _i32, _sz, _P]),
     "lisa_attn_build_info": (ctypes.c_char_p, []),
 }
 
