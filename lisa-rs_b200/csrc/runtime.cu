@@ -89,7 +89,10 @@ namespace lisa {
 namespace {
 std::atomic<uint64_t> g_fault_limit_ns{0};
 std::atomic<int> g_fault_withhold{0};
+std::atomic<int> g_prefill_split{0};
 }  // namespace
+
+int current_prefill_split() { return g_prefill_split.load(std::memory_order_relaxed); }
 
 WaitFault current_wait_fault() {
   return WaitFault{g_fault_limit_ns.load(std::memory_order_relaxed), g_fault_withhold.load(std::memory_order_relaxed)};
@@ -204,6 +207,7 @@ int lisa_attn_create(int device, int n_layers, uint32_t capacity, lisa_attn_ctx*
             cudaMalloc(&c->prefill_ws, c->prefill_ws_bytes) == cudaSuccess &&
             cudaMalloc(&c->err, sizeof(int)) == cudaSuccess && cudaMalloc(&c->sched, 64) == cudaSuccess;
   ok = ok && cudaMemset(c->k, 0, cache_bytes) == cudaSuccess && cudaMemset(c->v, 0, cache_bytes) == cudaSuccess &&
+       cudaMemset(c->prefill_ws, 0, c->prefill_ws_bytes) == cudaSuccess &&
        cudaMemset(c->err, 0, sizeof(int)) == cudaSuccess && cudaMemset(c->sched, 0, 64) == cudaSuccess &&
        cudaDeviceSynchronize() == cudaSuccess;
   // Tensor maps of every layer's K and V over the whole capacity (64-position
@@ -292,7 +296,7 @@ int lisa_attn_prefill_chunk(lisa_attn_ctx* c, int layer, uint32_t base, int rows
   p.capacity = c->capacity;
   p.base = base;
   p.rows = rows;
-  p.q_ws = reinterpret_cast<uint16_t*>(c->prefill_ws);
+  prefill_workspace_layout(c->prefill_ws, &p.q_ws, &p.part, &p.ready);
   p.gated_out = gated_out;
   p.err = c->err;
   return cuda_status(launch_prefill(p, c->num_sms, (cudaStream_t)stream));
@@ -445,6 +449,12 @@ int lisa_attn_window_check_device_error(void* workspace, void* stream) {
     return LISA_ECUDA;
   if (h && cudaMemsetAsync(workspace, 0, sizeof(int), st) != cudaSuccess) return LISA_ECUDA;
   return h ? LISA_ETIMEOUT : LISA_OK;
+}
+
+int lisa_attn_debug_prefill_split(int mode) {
+  if (mode < 0 || mode > 2) return LISA_EINVAL;
+  g_prefill_split.store(mode, std::memory_order_relaxed);
+  return LISA_OK;
 }
 
 int lisa_attn_debug_wait_fault(uint32_t wait_limit_us, int withhold_loads) {
