@@ -57,7 +57,7 @@ constexpr uint32_t PF_TMEM_S = 256;  // S / P tiles: columns [256, 384), [384, 5
 constexpr float PF_RESCALE_LOG2 = 8.0f;
 constexpr float kLog2Scale = SCALE * LOG2E;  // raw score -> exp2 argument
 constexpr uint16_t PF_PAIR = 3;  // multicast mask: both CTAs of the pair
-constexpr int PF_MAX_SEGMENTS = 8;  // clusters other than the finisher that share one unit
+constexpr int PF_MAX_PIECES = 24;   // pieces of one cluster's tile range (kept in shared memory)
 
 // mbarrier slots. *FULL, Q and PFULL are waited on by the pair's MMA issuer
 // (rank 0) and complete with both CTAs' loads / arrivals; SFULL and PVDONE
@@ -275,7 +275,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + PF_OFF_BAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + B_COUNT);
-  volatile uint32_t* seg_ok = tmem_slot + 1;  // finisher: every segment's partial arrived
+  volatile uint32_t* seg_ok = tmem_slot + 1;  // this CTA arrived last at a split unit
+  int* n_pieces_s = reinterpret_cast<int*>(smem + PF_OFF_BAR + 112);
+  PfPiece* pieces = reinterpret_cast<PfPiece*>(smem + PF_OFF_BAR + 128);  // [PF_MAX_PIECES]
   float* xmax = reinterpret_cast<float*>(smem + PF_OFF_BAR + 1024);  // [2 parity][2 half][128 rows]
   float* xsum = xmax + 2 * 2 * PF_BM;                                  // [2 half][128 rows]
 
@@ -295,6 +297,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
     tma_prefetch_desc(&tv);
     for (int b = 0; b < B_COUNT; ++b) mbar_init(&bars[b], (b == B_PFULL || b == B_PFULL + 1) ? 16 : 1);
     fence_mbar_init();
+    // the cluster's pieces, in order (the host keeps them within PF_MAX_PIECES)
+    PfPieces it{work, t_begin, t_end};
+    int np = 0;
+    PfPiece pc;
+    while (np < PF_MAX_PIECES && it.next(pc)) pieces[np++] = pc;
+    *n_pieces_s = np;
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, PF_TMEM_COLS);
@@ -309,11 +317,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
   // The setup above overlaps the prologue kernel; the K/V producers first
   // issue the loads of up to two key tiles of the first piece that hold only
   // positions below `base` (written by earlier calls), then wait too.
-  PfPiece first_pc;
-  {
-    PfPieces it{work, t_begin, t_end};
-    if (!it.next(first_pc)) first_pc = PfPiece{0, 0, 0, true, true};
-  }
+  const int n_pieces = *n_pieces_s;
+  const PfPiece first_pc = n_pieces ? pieces[0] : PfPiece{0, 0, 0, true, true};
   const int n_early = max(0, min(min(2, first_pc.j1 - first_pc.j0), (int)(p.base / PF_BN) - first_pc.j0));
   if (!((warp == 0 || warp == 2) && lane == 0)) pdl_wait_primary();
   pdl_launch_dependents();
@@ -339,11 +344,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
     // Each CTA loads its own 128 query rows and its half (64 keys) of every
     // K tile; completion is counted on rank 0's barriers, whose expected
     // byte count rank 0 sets for both.
-    PfPieces it{work, t_begin, t_end};
-    PfPiece pc;
-    int J = 0, pi = 0;
+    int J = 0;
     bool ok = true;
-    while (ok && it.next(pc)) {
+    for (int pi = 0; ok && pi < n_pieces; ++pi) {
+      const PfPiece pc = pieces[pi];
       const int qp = work.n_pairs - 1 - pc.unit / QH, h = pc.unit % QH, kvh = h / GQA;
       auto load_k = [&](int JJ, int j) {
         const int s = JJ & 1;
@@ -371,15 +375,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
         }
         load_k(J, j);
       }
-      ++pi;
     }
   } else if (warp == 2 && lane == 0) {
     // ---------------- V loads: this CTA's 128 dims of every V tile ----------------
-    PfPieces it{work, t_begin, t_end};
-    PfPiece pc;
-    int J = 0, pi = 0;
+    int J = 0;
     bool ok = true;
-    while (ok && it.next(pc)) {
+    for (int pi = 0; ok && pi < n_pieces; ++pi) {
+      const PfPiece pc = pieces[pi];
       const int kvh = (pc.unit % QH) / GQA;
       auto load_v = [&](int JJ, int j) {
         const int s = JJ & 1;
@@ -400,7 +402,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
         }
         load_v(J, j);
       }
-      ++pi;
     }
   } else if (warp == 1 && lane == 0 && rank == 0) {
     // ---------------- MMA issuer (rank 0 only, M = 256 over the pair) ----------------
@@ -430,11 +431,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
       return mbar_test_wait(&bars[B_PFULL + (J & 1)], (J >> 1) & 1) &&
              mbar_test_wait(&bars[B_VFULL + (J & 1)], (J >> 1) & 1);
     };
-    PfPieces it{work, t_begin, t_end};
-    PfPiece pc;
-    int J0 = 0, pi = 0;
+    int J0 = 0;
     bool ok = true;
-    while (ok && it.next(pc)) {
+    for (int pi = 0; ok && pi < n_pieces; ++pi) {
+      const PfPiece pc = pieces[pi];
       const int n = pc.j1 - pc.j0;
       ok = mbar_wait(&bars[B_Q], pi & 1, p.err, ERR_TIMEOUT_FULL) &&
            mbar_wait(&bars[B_KFULL + (J0 & 1)], (J0 >> 1) & 1, p.err, ERR_TIMEOUT_FULL);
@@ -474,7 +474,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
         umma_pair_commit(&bars[B_PVDONE + b], PF_PAIR);
       }
       J0 += n;
-      ++pi;
     }
     PT_FLUSH(0);
   } else if (warp >= 4) {
@@ -486,17 +485,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
     const int half = (warp - 4) >> 2;
     const int row = wi * 32 + lane;  // row within the CTA's tile == TMEM lane
     const uint32_t lane_addr = tmem + ((uint32_t)(wi * 32) << 16);
-    PfPieces it{work, t_begin, t_end};
-    PfPiece pc;
     int J0 = 0;
     bool ok = true;
-    while (ok && it.next(pc)) {
-      const int qp = work.n_pairs - 1 - pc.unit / QH, h = pc.unit % QH;
-      const int r0 = qp * 2 * PF_BM + (int)rank * PF_BM;
-      const int r = r0 + row;
-      const uint32_t pos_row = p.base + (uint32_t)r;
+    for (int pi = 0; ok && pi < n_pieces; ++pi) {
+      const PfPiece pc = pieces[pi];
+      const uint32_t pos_row =
+          p.base + (uint32_t)((work.n_pairs - 1 - pc.unit / QH) * 2 * PF_BM + (int)rank * PF_BM + row);
       const int n = pc.j1 - pc.j0;
-      const bool writes_out = pc.first && r < p.rows;
+      const int j0 = pc.j0;
       float mr = -INFINITY, l = 0.f;  // running max of the raw scores, this half's sum
       for (int i = 0; i < n; ++i) {
         const int J = J0 + i, b = J & 1;
@@ -515,7 +511,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
         float x[64];  // raw scores Q.K (unscaled)
 #pragma unroll
         for (int c = 0; c < 64; ++c) x[c] = __uint_as_float(c < 32 ? sa[c] : sb[c - 32]);
-        const uint32_t key0 = (uint32_t)(pc.j0 + i) * PF_BN + half * 64;
+        const uint32_t key0 = (uint32_t)(j0 + i) * PF_BN + half * 64;
         if (key0 + 63 > pos_row) {  // diagonal tile: keys past this row's position
 #pragma unroll
           for (int c = 0; c < 64; ++c)
@@ -592,20 +588,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
         PT(4);
       }
       if (!ok) break;
-      // Gate values of this row and half, rounded to bf16 as the reference
-      // does; their loads overlap the last P.V.
-      uint32_t gpk[64];
-      if (writes_out) {
-        const size_t gbase = (size_t)r * QROW + (size_t)h * 512 + 256 + half * 128;
-#pragma unroll
-        for (int g8 = 0; g8 < 16; ++g8) {
-          const uint4 w4 = load8_bf16(p.q_gate, gbase + g8 * 8, p.in_bf16);
-          gpk[4 * g8] = w4.x;
-          gpk[4 * g8 + 1] = w4.y;
-          gpk[4 * g8 + 2] = w4.z;
-          gpk[4 * g8 + 3] = w4.w;
-        }
-      }
       const int Jl = J0 + n - 1;
       J0 += n;
       ok = mbar_wait(&bars[B_PVDONE + (Jl & 1)], (Jl >> 1) & 1, p.err, ERR_TIMEOUT_MMA);
@@ -616,10 +598,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
       const float l_row = xsum[row] + xsum[PF_BM + row];
       named_bar_sync(2 + wi, 64);  // both halves have read xsum before the next piece writes it
       tc_fence_after();
-      if (!pc.first) {
-        // ---- a continuation of a unit another cluster started: leave the
-        // partial (unnormalised O of this half, max, row sum) for it ----
-        float* dst = p.part + (((size_t)cl * 2 + rank) * PF_BM + row) * PF_PART_STRIDE;
+      const PfPiece pe = pieces[pi];
+      float den = l_row;
+      if (!(pe.first && pe.last)) {
+        // ---- a unit split over clusters c_first .. c_last. Every segment
+        // leaves its partial (unnormalised O of this CTA's rows, max, row
+        // sum); the last one to finish (counted per unit and rank) merges all
+        // of them in cluster order, so the result does not depend on which
+        // cluster arrives last. Nobody waits, so the clusters need not be
+        // resident at the same time. ----
+        const int u_off = work.unit_off(pe.unit), u_end = u_off + work.unit_tiles(pe.unit);
+        int c_first = cl, c_last = cl;
+        while (c_first > 0 && work.range_start(c_first) > u_off) --c_first;
+        while (c_last + 1 < work.clusters && work.range_start(c_last + 1) < u_end) ++c_last;
+        // a segment's slot: its cluster's first piece (which 0) or, for the
+        // cluster whose range starts before the unit, its last piece (1)
+        auto slot_ptr = [&](int c) -> float* {
+          const int which = work.range_start(c) < u_off ? 1 : 0;
+          return p.part + ((((size_t)c * 2 + which) * 2 + rank) * PF_BM + row) * PF_PART_STRIDE;
+        };
+        float* dst = slot_ptr(cl);
 #pragma unroll 1
         for (int c = 0; c < HD / 64; ++c) {
           const int col = half * (HD / 2) + c * 32;
@@ -628,70 +626,43 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
           tmem_wait_ld();
 #pragma unroll
           for (int q = 0; q < 8; ++q)
-            *reinterpret_cast<uint4*>(dst + col + 4 * q) = make_uint4(ov[4 * q], ov[4 * q + 1], ov[4 * q + 2],
-                                                                      ov[4 * q + 3]);
+            __stcg(reinterpret_cast<uint4*>(dst + col + 4 * q),
+                   make_uint4(ov[4 * q], ov[4 * q + 1], ov[4 * q + 2], ov[4 * q + 3]));
         }
-        if (half == 0) *reinterpret_cast<float2*>(dst + HD) = make_float2(mr, l_row);
-        tc_fence_before();
+        if (half == 0) __stcg(reinterpret_cast<float2*>(dst + HD), make_float2(mr, l_row));
         __threadfence();
         named_bar_sync(6, 256);  // the whole partial of this CTA is written
-        if (threadIdx.x == 128) st_release_gpu(p.ready + cl * 2 + rank, 1u);
-        continue;
-      }
-      // ---- this cluster holds the unit's first tile: it writes the output,
-      // merging the partials of the clusters that ran the unit's other tiles ----
-      float den = l_row;
-      if (!pc.last) {
-        const int u_end = work.unit_off(pc.unit) + work.unit_tiles(pc.unit);
-        int n_src = 0;  // the clusters cl + 1 .. cl + n_src ran the unit's other tiles
-        while (cl + 1 + n_src < work.clusters && work.range_start(cl + 1 + n_src) < u_end) ++n_src;
         if (threadIdx.x == 128) {
-          if (n_src > PF_MAX_SEGMENTS) {  // the host never splits a unit this finely
-            atomicExch(p.err, ERR_TIMEOUT_MMA);
-            ok = false;
-          }
-          for (int k2 = 0; ok && k2 < n_src; ++k2) {
-            uint32_t* f = p.ready + (cl + 1 + k2) * 2 + rank;
-            const uint64_t t0 = global_timer_ns();
-            while (ld_acquire_gpu(f) == 0u) {
-              if (global_timer_ns() - t0 > WAIT_LIMIT_NS) {
-                atomicExch(p.err, ERR_TIMEOUT_MMA);
-                ok = false;
-                break;
-              }
-              __nanosleep(32);
-            }
-            if (ok) *f = 0u;  // consumed: the next call's writer starts from zero
-          }
-          *seg_ok = ok ? 1u : 0u;
+          uint32_t* cnt = p.ready + pe.unit * 2 + rank;
+          const uint32_t before = atomicAdd(cnt, 1u);
+          const bool last = before == (uint32_t)(c_last - c_first);
+          if (last) *cnt = 0u;  // every segment has arrived: ready for the next call
+          __threadfence();
+          *seg_ok = last ? 1u : 0u;
         }
         named_bar_sync(6, 256);
-        ok = *seg_ok != 0u;
+        const bool merge = *seg_ok != 0u;
         named_bar_sync(6, 256);
-        if (!ok) break;
-        // Merge the other segments' partials into this piece's O in TMEM:
-        // O = O_self * w_self + sum_k O_k * w_k with w = 2^((m - m_all) c).
-        const float* base_ptr = p.part + ((size_t)(cl + 1) * 2 + rank) * PF_BM * PF_PART_STRIDE +
-                                (size_t)row * PF_PART_STRIDE;
-        const size_t seg_stride = (size_t)2 * PF_BM * PF_PART_STRIDE;
-        float mall = mr;
-        for (int k2 = 0; k2 < n_src; ++k2) mall = fmaxf(mall, __ldcg(base_ptr + k2 * seg_stride + HD));
-        const float wself = mr == -INFINITY ? 0.f : fast_exp2((mr - mall) * kLog2Scale);
-        den = l_row * wself;
-        for (int k2 = 0; k2 < n_src; ++k2) {
-          const float2 ml = __ldcg(reinterpret_cast<const float2*>(base_ptr + k2 * seg_stride + HD));
+        if (!merge) {
+          tc_fence_before();
+          continue;
+        }
+        // O = sum_s O_s * w_s, den = sum_s l_s * w_s, w_s = 2^((m_s - m_all) c)
+        float mall = -INFINITY;
+        for (int c = c_first; c <= c_last; ++c) mall = fmaxf(mall, __ldcg(slot_ptr(c) + HD));
+        den = 0.f;
+        for (int c = c_first; c <= c_last; ++c) {
+          const float2 ml = __ldcg(reinterpret_cast<const float2*>(slot_ptr(c) + HD));
           den += ml.y * (ml.x == -INFINITY ? 0.f : fast_exp2((ml.x - mall) * kLog2Scale));
         }
 #pragma unroll 1
         for (int c = 0; c < HD / 64; ++c) {
           const int col = half * (HD / 2) + c * 32;
           uint32_t ov[32];
-          tmem_ld32(lane_addr + PF_TMEM_O + col, ov);
-          tmem_wait_ld();
 #pragma unroll
-          for (int q = 0; q < 32; ++q) ov[q] = __float_as_uint(__uint_as_float(ov[q]) * wself);
-          for (int k2 = 0; k2 < n_src; ++k2) {
-            const float* sp = base_ptr + k2 * seg_stride;
+          for (int q = 0; q < 32; ++q) ov[q] = 0u;
+          for (int cc = c_first; cc <= c_last; ++cc) {
+            const float* sp = slot_ptr(cc);
             const float mk = __ldcg(sp + HD);
             const float wk = mk == -INFINITY ? 0.f : fast_exp2((mk - mall) * kLog2Scale);
             const float4* s4 = reinterpret_cast<const float4*>(sp + col);
@@ -708,26 +679,47 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
         }
         tmem_wait_st();
       }
-      if (writes_out) {
+      // ---- gated output of the unit's rows: O / den * sigmoid(gate). Every
+      // lane takes part in the TMEM loads (warp-collective); rows past the
+      // chunk only skip their gate loads and stores. ----
+      {
+        const int h = pe.unit % QH;
+        const int r = (work.n_pairs - 1 - pe.unit / QH) * 2 * PF_BM + (int)rank * PF_BM + row;
+        const bool valid = r < p.rows;
         const float inv_l = 1.0f / den;
+        const size_t gbase = (size_t)r * QROW + (size_t)h * 512 + 256 + half * 128;
         uint16_t* out = p.gated_out + (size_t)r * OROW + (size_t)h * HD + half * (HD / 2);
+        uint4 g4[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          g4[q] = valid ? load8_bf16(p.q_gate, gbase + 8 * q, p.in_bf16) : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
         for (int c = 0; c < HD / 64; ++c) {
           const int col = half * (HD / 2) + c * 32;
           uint32_t ov[32];
           tmem_ld32(lane_addr + PF_TMEM_O + col, ov);
+          uint4 gn[4];  // the next 32 dims' gate, in flight during this pass
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            gn[q] = (valid && c + 1 < HD / 64) ? load8_bf16(p.q_gate, gbase + 32 * (c + 1) + 8 * q, p.in_bf16)
+                                               : make_uint4(0u, 0u, 0u, 0u);
           tmem_wait_ld();
           uint32_t outw[16];
 #pragma unroll
           for (int q = 0; q < 16; ++q) {
-            const float2 g2 = unpack_bf16x2(gpk[c * 16 + q]);
+            const uint32_t gw = (&g4[q >> 2].x)[q & 3];
+            const float2 g2 = unpack_bf16x2(gw);
             outw[q] = pack_bf16x2(__uint_as_float(ov[2 * q]) * inv_l * fast_sigmoid(g2.x),
                                   __uint_as_float(ov[2 * q + 1]) * inv_l * fast_sigmoid(g2.y));
           }
+          if (valid) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            *reinterpret_cast<uint4*>(out + c * 32 + 8 * q) =
-                make_uint4(outw[4 * q], outw[4 * q + 1], outw[4 * q + 2], outw[4 * q + 3]);
+            for (int q = 0; q < 4; ++q)
+              *reinterpret_cast<uint4*>(out + c * 32 + 8 * q) =
+                  make_uint4(outw[4 * q], outw[4 * q + 1], outw[4 * q + 2], outw[4 * q + 3]);
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) g4[q] = gn[q];
         }
       }
       tc_fence_before();
@@ -748,7 +740,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
 
 namespace {
 constexpr size_t PF_QWS_BYTES = (size_t)QH * PF_MAX_ROWS * HD * sizeof(uint16_t);
-constexpr size_t PF_PART_BYTES = (size_t)PF_MAX_CLUSTERS * 2 * PF_BM * PF_PART_STRIDE * sizeof(float);
+constexpr size_t PF_PART_BYTES = (size_t)PF_MAX_CLUSTERS * 2 * 2 * PF_BM * PF_PART_STRIDE * sizeof(float);
 }  // namespace
 
 size_t prefill_workspace_bytes() { return PF_QWS_BYTES + PF_PART_BYTES + PF_MAX_CLUSTERS * 2 * sizeof(uint32_t); }
@@ -821,12 +813,13 @@ cudaError_t launch_prefill(const PrefillParams& p_in, int num_sms, cudaStream_t 
   const int n_qt = (p.rows + PF_BM - 1) / PF_BM;
   const int n_pairs = (n_qt + 1) / 2;
   const int units = n_pairs * QH;
-  int total = 0, longest = 0;
+  int total = 0, longest = 0, shortest = 1 << 30;
   for (int qp = 0; qp < n_pairs; ++qp) {
     const int end = std::min(qp * 2 * PF_BM + 2 * PF_BM, p.rows);
     const int n = (int)((p.base + (uint32_t)end + PF_BN - 1) / PF_BN);
     total += QH * n;
     longest = std::max(longest, n);
+    shortest = std::min(shortest, n);
   }
   // Stream-K clusters wait for one another's partials, so all of them must be
   // resident at once: at most the number of 2-CTA clusters of this kernel the
@@ -835,7 +828,8 @@ cudaError_t launch_prefill(const PrefillParams& p_in, int num_sms, cudaStream_t 
   const int share = (total + slots - 1) / slots;
   p.total_tiles = total;
   const int mode = current_prefill_split();
-  if (units < slots && (mode == 2 || (mode == 0 && share + 2 < longest))) {
+  const bool fits = (share + shortest - 1) / shortest + 2 <= PF_MAX_PIECES;  // pieces per cluster
+  if (units < slots && fits && (mode == 2 || (mode == 0 && share + 2 < longest))) {
     p.streamk = 1;
     p.clusters = slots;
   } else {

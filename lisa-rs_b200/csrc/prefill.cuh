@@ -19,7 +19,7 @@ namespace lisa {
 
 constexpr int PF_MAX_ROWS = 512;
 constexpr int PF_PART_STRIDE = 260;   // floats per row of a split partial: O[256], max, sum, 2 pad
-constexpr int PF_MAX_CLUSTERS = 128;  // stream-K clusters (one per 2 SMs)
+constexpr int PF_MAX_CLUSTERS = 96;  // stream-K clusters (one per 2 SMs)
 
 struct PrefillParams {
   const void* q_gate;  // [rows][24][512]
@@ -41,14 +41,14 @@ struct PrefillParams {
   // rows, head); its key tiles are numbered 0 .. tiles-1; units are ordered
   // heaviest first and their tiles concatenated into one list of
   // total_tiles. streamk = 0: cluster c runs unit c. streamk = 1: cluster c
-  // runs tiles [c*total/clusters, (c+1)*total/clusters) of the list, and a
-  // unit split over several clusters is finished by the cluster holding its
-  // first tile, from the others' partials.
+  // runs tiles [c*total/clusters, (c+1)*total/clusters) of the list; every
+  // cluster holding part of a split unit leaves a partial and the last one
+  // to finish merges them.
   int streamk;
   int clusters;
   int total_tiles;
-  float* part;       // [clusters][2 ranks][128 rows][PF_PART_STRIDE] f32: O (unnormalised), max, sum
-  uint32_t* ready;   // [clusters][2 ranks]: 1 = that partial is written (reset by its reader)
+  float* part;       // [clusters][2: first / last piece][2 ranks][128 rows][PF_PART_STRIDE]: O, max, sum
+  uint32_t* ready;   // [units][2 ranks]: segments of a split unit that have finished (reset by the last)
   float inv_freq[32];  // filled by launch_prefill
 #if defined(LISA_PREFILL_TRACE) || defined(LISA_PREFILL_OBSERVE)
   unsigned long long* trace;  // debug builds only
