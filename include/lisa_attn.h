@@ -329,13 +329,6 @@ int lisa_attn_copy_d2h(void* dst, const void* src, size_t bytes, void* stream);
 int lisa_attn_copy_d2d(void* dst, const void* src, size_t bytes, void* stream);
 int lisa_attn_memset(void* dst, int value, size_t bytes, void* stream);
 
-/* Test hook, no lisa-rs counterpart. Process-wide work split of later
- * prefill launches: 0 = chosen per call (default), 1 = one cluster per
- * (query-row pair, head), 2 = stream-K (equal key-tile shares over every
- * cluster slot of the GPU) whenever there are more slots than units. Results
- * agree within the decode tolerance, not bit for bit. LISA_EINVAL otherwise. */
-int lisa_attn_debug_prefill_split(int mode);
-
 /* Library build identification (for tests: the .so in use). */
 const char* lisa_attn_build_info(void);
 

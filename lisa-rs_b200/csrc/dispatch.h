@@ -64,9 +64,4 @@ struct WaitFault {
 };
 WaitFault current_wait_fault();
 
-// Test hook (lisa_attn_debug_prefill_split): 0 = the launch chooses the
-// prefill work split, 1 = one cluster per unit, 2 = stream-K whenever the GPU
-// has more cluster slots than units.
-int current_prefill_split();
-
 }  // namespace lisa

@@ -30,7 +30,6 @@
 //                one TMA store.
 // Key tiles past the pair's last query row are skipped (causal tile skipping).
 #include <algorithm>
-#include <mutex>
 
 #include "common.cuh"
 #include "prefill.cuh"
@@ -57,7 +56,6 @@ constexpr uint32_t PF_TMEM_S = 256;  // S / P tiles: columns [256, 384), [384, 5
 constexpr float PF_RESCALE_LOG2 = 8.0f;
 constexpr float kLog2Scale = SCALE * LOG2E;  // raw score -> exp2 argument
 constexpr uint16_t PF_PAIR = 3;  // multicast mask: both CTAs of the pair
-constexpr int PF_MAX_PIECES = 24;   // pieces of one cluster's tile range (kept in shared memory)
 
 // mbarrier slots. *FULL, Q and PFULL are waited on by the pair's MMA issuer
 // (rank 0) and complete with both CTAs' loads / arrivals; SFULL and PVDONE
@@ -206,87 +204,31 @@ __global__ void __launch_bounds__(256, 4) prefill_prologue_kernel(const PrefillP
 #endif
 }
 
-// The work list of one call: units (query-row pair qp, head h) heaviest first,
-// unit u -> qp = n_pairs - 1 - u / 24, h = u % 24; its key tiles 0..n(qp)-1.
-struct PfWork {
-  int n_pairs, rows;
-  uint32_t base;
-  int streamk, clusters, total;
-  __device__ __forceinline__ int qp_tiles(int qp) const {
-    const int end = min(qp * 2 * PF_BM + 2 * PF_BM, rows);
-    return (int)((base + (uint32_t)end + PF_BN - 1) / PF_BN);
-  }
-  __device__ __forceinline__ int unit_tiles(int u) const { return qp_tiles(n_pairs - 1 - u / QH); }
-  __device__ __forceinline__ int unit_off(int u) const {
-    const int g = u / QH;
-    int off = 0;
-    for (int k = 0; k < g; ++k) off += QH * qp_tiles(n_pairs - 1 - k);
-    return off + (u % QH) * qp_tiles(n_pairs - 1 - g);
-  }
-  __device__ __forceinline__ int unit_at(int t) const {
-    int off = 0;
-    for (int g = 0; g < n_pairs; ++g) {
-      const int n = qp_tiles(n_pairs - 1 - g);
-      if (t < off + QH * n) return g * QH + (t - off) / n;
-      off += QH * n;
-    }
-    return -1;
-  }
-  // first tile of cluster c's range (c == clusters gives the end of the list)
-  __device__ __forceinline__ int range_start(int c) const {
-    if (streamk) return (int)(((int64_t)c * total) / clusters);
-    return c >= clusters ? total : unit_off(c);
-  }
-};
-
-// One contiguous run of a unit's key tiles inside a cluster's range.
-struct PfPiece {
-  int unit, j0, j1;  // tiles [j0, j1) of the unit
-  bool first, last;  // holds the unit's first / last tile
-};
-
-struct PfPieces {
-  const PfWork& w;
-  int t, t_end;
-  __device__ __forceinline__ bool next(PfPiece& pc) {
-    if (t >= t_end) return false;
-    const int u = w.unit_at(t);
-    const int off = w.unit_off(u), n = w.unit_tiles(u);
-    pc.unit = u;
-    pc.j0 = t - off;
-    pc.j1 = min(n, t_end - off);
-    pc.first = pc.j0 == 0;
-    pc.last = pc.j1 == n;
-    t = off + pc.j1;
-    return true;
-  }
-};
-
-// Persistent attention: each cluster of two CTAs runs the pieces of its tile
-// range in order. Cluster rank 0 holds query rows [256 qp, 256 qp + 128) of a
-// unit, rank 1 the next 128. Tiles are numbered J = 0, 1, ... across the
-// cluster's pieces so that the ring barriers' phases continue from piece to
-// piece; query tile, accumulator and running softmax state restart with every
-// piece.
+// Grid: clusters of 2 CTAs, n_pairs * 24 clusters, heaviest (last) query
+// row pairs first. Cluster rank 0 holds query rows [256 qp, 256 qp + 128),
+// rank 1 the next 128.
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
     prefill_attn_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                        const __grid_constant__ CUtensorMap tv, const PrefillParams p) {
+                        const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tg,
+                        const __grid_constant__ CUtensorMap to, const PrefillParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + PF_OFF_BAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + B_COUNT);
-  volatile uint32_t* seg_ok = tmem_slot + 1;  // this CTA arrived last at a split unit
-  int* n_pieces_s = reinterpret_cast<int*>(smem + PF_OFF_BAR + 112);
-  PfPiece* pieces = reinterpret_cast<PfPiece*>(smem + PF_OFF_BAR + 128);  // [PF_MAX_PIECES]
   float* xmax = reinterpret_cast<float*>(smem + PF_OFF_BAR + 1024);  // [2 parity][2 half][128 rows]
   float* xsum = xmax + 2 * 2 * PF_BM;                                  // [2 half][128 rows]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
-  const int cl = (int)(blockIdx.x >> 1);
   const int n_qt = (p.rows + PF_BM - 1) / PF_BM;
-  const PfWork work{(n_qt + 1) / 2, p.rows, p.base, p.streamk, p.clusters, p.total_tiles};
-  const int t_begin = work.range_start(cl), t_end = work.range_start(cl + 1);
+  const int n_pairs = (n_qt + 1) / 2;
+  const int cl = (int)(blockIdx.x >> 1);
+  const int qp = n_pairs - 1 - cl / QH;
+  const int h = cl % QH, kvh = h / GQA;
+  const int r0 = qp * 2 * PF_BM + (int)rank * PF_BM;
+  const int pair_end = min(qp * 2 * PF_BM + 2 * PF_BM, p.rows);
+  const uint32_t kv_end = p.base + (uint32_t)pair_end;  // keys [0, kv_end) for both CTAs
+  const int n_tiles = (int)((kv_end + PF_BN - 1) / PF_BN);
 
 #ifdef LISA_PREFILL_TRACE
   if (threadIdx.x == 0) p.trace[64 + blockIdx.x * 8 + 0] = global_timer_ns();
@@ -295,14 +237,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
     tma_prefetch_desc(&tq);
     tma_prefetch_desc(&tk);
     tma_prefetch_desc(&tv);
+    tma_prefetch_desc(&to);
     for (int b = 0; b < B_COUNT; ++b) mbar_init(&bars[b], (b == B_PFULL || b == B_PFULL + 1) ? 16 : 1);
     fence_mbar_init();
-    // the cluster's pieces, in order (the host keeps them within PF_MAX_PIECES)
-    PfPieces it{work, t_begin, t_end};
-    int np = 0;
-    PfPiece pc;
-    while (np < PF_MAX_PIECES && it.next(pc)) pieces[np++] = pc;
-    *n_pieces_s = np;
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, PF_TMEM_COLS);
@@ -312,17 +249,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
   cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // shared::cluster address of rank 0's barrier `i`
   const uint32_t lead_bars = cluster_map(smem_u32(bars), 0);
   auto lead_bar = [&](int i) -> uint32_t { return lead_bars + 8u * (uint32_t)i; };
-  // The setup above overlaps the prologue kernel; the K/V producers first
-  // issue the loads of up to two key tiles of the first piece that hold only
-  // positions below `base` (written by earlier calls), then wait too.
-  const int n_pieces = *n_pieces_s;
-  const PfPiece first_pc = n_pieces ? pieces[0] : PfPiece{0, 0, 0, true, true};
-  const int n_early = max(0, min(min(2, first_pc.j1 - first_pc.j0), (int)(p.base / PF_BN) - first_pc.j0));
+  // Setup above overlaps the prologue kernel; its q_ws / KV writes are read
+  // only after it has completed. The K/V producers first issue the loads of
+  // the first two key tiles when they hold only positions below `base`
+  // (written by earlier calls), then wait too.
+  const int n_early = min(min(2, n_tiles), (int)(p.base / PF_BN));
   if (!((warp == 0 || warp == 2) && lane == 0)) pdl_wait_primary();
   pdl_launch_dependents();
 #ifdef LISA_PREFILL_TRACE
+  if (threadIdx.x == 0) p.trace[64 + blockIdx.x * 8 + 1] = global_timer_ns();
   unsigned long long tr[8] = {};
   long long tl = clock64();
 #define PT(k)                        \
@@ -334,9 +272,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
 #define PT_FLUSH(role)                                                             \
   if (lane == 0)                                                                   \
     for (int k = 0; k < 8; ++k) atomicAdd(&p.trace[(role) * 8 + k], tr[k]);
+// per-tile event clocks of the first CTA (rank 0 of the heaviest pair)
+#define PE(ev, j) \
+  if (blockIdx.x == 0 && (j) < 64) p.trace[2048 + (ev) * 64 + (j)] = clock64();
 #else
 #define PT(k)
 #define PT_FLUSH(role)
+#define PE(ev, j)
 #endif
 
   if (warp == 0 && lane == 0) {
@@ -344,139 +286,130 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
     // Each CTA loads its own 128 query rows and its half (64 keys) of every
     // K tile; completion is counted on rank 0's barriers, whose expected
     // byte count rank 0 sets for both.
-    int J = 0;
-    bool ok = true;
-    for (int pi = 0; ok && pi < n_pieces; ++pi) {
-      const PfPiece pc = pieces[pi];
-      const int qp = work.n_pairs - 1 - pc.unit / QH, h = pc.unit % QH, kvh = h / GQA;
-      auto load_k = [&](int JJ, int j) {
-        const int s = JJ & 1;
-        if (rank == 0) mbar_arrive_expect_tx(&bars[B_KFULL + s], 2 * PF_KH_BYTES);
-        tma_load_4d_pair(smem + PF_OFF_K + s * PF_KH_BYTES, &tk, lead_bar(B_KFULL + s), 0,
-                         j * PF_BN + (int)rank * (PF_BN / 2), 0, kvh);
-      };
-      int j = pc.j0;
-      if (pi == 0) {
-        for (; j < pc.j0 + n_early; ++j, ++J) load_k(J, j);
-        pdl_wait_primary();
-      } else {
-        // the query tile is overwritten once the previous piece's last S,
-        // which read it, has completed
-        ok = mbar_wait(&bars[B_SFULL + ((J - 1) & 1)], ((J - 1) >> 1) & 1, p.err, ERR_TIMEOUT_EMPTY);
-        if (!ok) break;
-      }
-      if (rank == 0) mbar_arrive_expect_tx(&bars[B_Q], 2 * PF_Q_BYTES);
-      tma_load_4d_pair(smem, &tq, lead_bar(B_Q), 0, qp * 2 * PF_BM + (int)rank * PF_BM, 0, h);
-      for (; j < pc.j1; ++j, ++J) {
-        // slot J & 1 is free once S_{J-2}, which read it, has completed
-        if (J >= 2 && !mbar_wait(&bars[B_SFULL + (J & 1)], ((J >> 1) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) {
-          ok = false;
-          break;
-        }
-        load_k(J, j);
+    auto load_k = [&](int j) {
+      const int s = j & 1;
+      if (rank == 0) mbar_arrive_expect_tx(&bars[B_KFULL + s], 2 * PF_KH_BYTES);
+      tma_load_4d_pair(smem + PF_OFF_K + s * PF_KH_BYTES, &tk, lead_bar(B_KFULL + s), 0,
+                       j * PF_BN + (int)rank * (PF_BN / 2), 0, kvh);
+    };
+    for (int j = 0; j < n_early; ++j) load_k(j);
+    pdl_wait_primary();
+    if (rank == 0) mbar_arrive_expect_tx(&bars[B_Q], 2 * PF_Q_BYTES);
+    tma_load_4d_pair(smem, &tq, lead_bar(B_Q), 0, r0, 0, h);
+    for (int j = n_early; j < n_tiles; ++j) {
+      // slot j & 1 is free once S_{j-2}, which read it, has completed
+      if (j >= 2 && !mbar_wait(&bars[B_SFULL + (j & 1)], ((j >> 1) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) break;
+      load_k(j);
+    }
+    if (p.in_bf16) {
+      // once the last two S MMAs have read the K ring, it takes this CTA's
+      // gate tile: rows r0.., gate dims 256..511 of head h
+      bool free = true;
+      for (int j = max(0, n_tiles - 2); free && j < n_tiles; ++j)
+        free = mbar_wait(&bars[B_SFULL + (j & 1)], (j >> 1) & 1, p.err, ERR_TIMEOUT_EMPTY);
+      if (free) {
+        mbar_arrive_expect_tx(&bars[B_G], PF_BM * HD * 2);
+        tma_load_4d(smem + PF_OFF_K, &tg, &bars[B_G], 0, r0, 4, h);
       }
     }
   } else if (warp == 2 && lane == 0) {
     // ---------------- V loads: this CTA's 128 dims of every V tile ----------------
-    int J = 0;
-    bool ok = true;
-    for (int pi = 0; ok && pi < n_pieces; ++pi) {
-      const PfPiece pc = pieces[pi];
-      const int kvh = (pc.unit % QH) / GQA;
-      auto load_v = [&](int JJ, int j) {
-        const int s = JJ & 1;
-        if (rank == 0) mbar_arrive_expect_tx(&bars[B_VFULL + s], 2 * PF_VH_BYTES);
-        tma_load_4d_pair(smem + PF_OFF_V + s * PF_VH_BYTES, &tv, lead_bar(B_VFULL + s), 0, j * PF_BN,
-                         2 * (int)rank, kvh);
-      };
-      int j = pc.j0;
-      if (pi == 0) {
-        for (; j < pc.j0 + n_early; ++j, ++J) load_v(J, j);
-        pdl_wait_primary();
-      }
-      for (; j < pc.j1; ++j, ++J) {
-        // slot J & 1 is free once P_{J-2}.V_{J-2}, which read it, has completed
-        if (J >= 2 && !mbar_wait(&bars[B_PVDONE + (J & 1)], ((J >> 1) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) {
-          ok = false;
-          break;
-        }
-        load_v(J, j);
-      }
+    auto load_v = [&](int j) {
+      const int s = j & 1;
+      if (rank == 0) mbar_arrive_expect_tx(&bars[B_VFULL + s], 2 * PF_VH_BYTES);
+      tma_load_4d_pair(smem + PF_OFF_V + s * PF_VH_BYTES, &tv, lead_bar(B_VFULL + s), 0, j * PF_BN,
+                       2 * (int)rank, kvh);
+    };
+    for (int j = 0; j < n_early; ++j) load_v(j);
+    pdl_wait_primary();
+    for (int j = n_early; j < n_tiles; ++j) {
+      // slot j & 1 is free once P_{j-2}.V_{j-2}, which read it, has completed
+      if (j >= 2 && !mbar_wait(&bars[B_PVDONE + (j & 1)], ((j >> 1) - 1) & 1, p.err, ERR_TIMEOUT_EMPTY)) break;
+      load_v(j);
     }
   } else if (warp == 1 && lane == 0 && rank == 0) {
     // ---------------- MMA issuer (rank 0 only, M = 256 over the pair) ----------------
     // The tensor pipe keeps almost no queue: every cycle this thread spends
-    // between two MMAs is a cycle the pipe idles. Inside a piece the group
-    // sequence S_0, S_1, PV_0, S_2, PV_1, ... is issued without waits between
-    // groups (the next group's inputs are tested before the current group's
-    // last MMA); at a piece boundary the last P.V goes first, then the next
-    // piece's first S once its query tile has landed.
+    // between two MMAs is a cycle the pipe idles. So the group sequence
+    // S_0, S_1, PV_0, S_2, PV_1, ... is issued without waits between groups:
+    // the inputs of the next group are tested (non-blocking) before the last
+    // MMA of the current group, and descriptors are base + constant offsets.
     constexpr uint32_t IDESC_S = umma_idesc_bf16(2 * PF_BM, PF_BN, false);
     constexpr uint32_t IDESC_O = umma_idesc_bf16(2 * PF_BM, HD, true);
+    // S_j = Q . K_j^T: 16 k-steps of 16 dims; Q rows and K keys are stored as
+    // [64-dim group][row][64 dims]. O += P_j . V_j: 8 k-steps of 16 keys; P
+    // (bf16 pairs) lives over the S tile, key k at column k/2; V is stored
+    // [64-dim group][key][64 dims] and read MN-major (this CTA holds 2 of the
+    // 4 groups).
     const uint64_t dQ = umma_desc_sw128(smem_u32(smem), 16, 1024);
     const uint64_t dK = umma_desc_sw128(smem_u32(smem + PF_OFF_K), 16, 1024);
     const uint64_t dV = umma_desc_sw128(smem_u32(smem + PF_OFF_V), PF_BN * 128, 1024);
-    auto s_mma = [&](int J, int kk) {
-      const uint32_t g = kk >> 2, sub = kk & 3, s = J & 1;
+    auto s_mma = [&](int j, int kk) {
+      const uint32_t g = kk >> 2, sub = kk & 3, s = j & 1;
       umma_pair_bf16(tmem + PF_TMEM_S + s * PF_BN, dQ + ((g * (PF_BM * 128) + sub * 32) >> 4),
                      dK + ((s * PF_KH_BYTES + g * ((PF_BN / 2) * 128) + sub * 32) >> 4), IDESC_S, kk ? 1u : 0u);
     };
-    auto pv_mma = [&](int J, bool acc, int kk) {
-      const uint32_t b = J & 1;
+    auto pv_mma = [&](int j, int kk) {
+      const uint32_t b = j & 1;
       umma_pair_bf16_ts(tmem + PF_TMEM_O, tmem + PF_TMEM_S + b * PF_BN + kk * 8,
-                        dV + ((b * PF_VH_BYTES + kk * 2048) >> 4), IDESC_O, (acc || kk > 0) ? 1u : 0u);
+                        dV + ((b * PF_VH_BYTES + kk * 2048) >> 4), IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
     };
-    auto k_ready = [&](int J) { return mbar_test_wait(&bars[B_KFULL + (J & 1)], (J >> 1) & 1); };
-    auto pv_ready = [&](int J) {
-      return mbar_test_wait(&bars[B_PFULL + (J & 1)], (J >> 1) & 1) &&
-             mbar_test_wait(&bars[B_VFULL + (J & 1)], (J >> 1) & 1);
+    auto k_ready = [&](int j) { return mbar_test_wait(&bars[B_KFULL + (j & 1)], (j >> 1) & 1); };
+    auto pv_ready = [&](int j) {
+      return mbar_test_wait(&bars[B_PFULL + (j & 1)], (j >> 1) & 1) &&
+             mbar_test_wait(&bars[B_VFULL + (j & 1)], (j >> 1) & 1);
     };
-    int J0 = 0;
-    bool ok = true;
-    for (int pi = 0; ok && pi < n_pieces; ++pi) {
-      const PfPiece pc = pieces[pi];
-      const int n = pc.j1 - pc.j0;
-      ok = mbar_wait(&bars[B_Q], pi & 1, p.err, ERR_TIMEOUT_FULL) &&
-           mbar_wait(&bars[B_KFULL + (J0 & 1)], (J0 >> 1) & 1, p.err, ERR_TIMEOUT_FULL);
-      if (!ok) break;
+    bool ok = mbar_wait(&bars[B_Q], 0, p.err, ERR_TIMEOUT_FULL) &&
+              mbar_wait(&bars[B_KFULL], 0, p.err, ERR_TIMEOUT_FULL);
+    if (ok) {
       tc_fence_after();
 #pragma unroll
-      for (int kk = 0; kk < 16; ++kk) s_mma(J0, kk);
-      umma_pair_commit(&bars[B_SFULL + (J0 & 1)], PF_PAIR);
-      bool next_ready = false;  // inputs of the next group already seen complete
-      for (int i = 0; ok && i < n; ++i) {
-        const int J = J0 + i, b = J & 1;
-        if (i + 1 < n) {
-          if (!next_ready &&
-              !mbar_wait(&bars[B_KFULL + ((J + 1) & 1)], ((J + 1) >> 1) & 1, p.err, ERR_TIMEOUT_FULL)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < 15; ++kk) s_mma(J + 1, kk);
-          next_ready = pv_ready(J);
-          s_mma(J + 1, 15);
-          umma_pair_commit(&bars[B_SFULL + ((J + 1) & 1)], PF_PAIR);
-        } else {
-          next_ready = false;
-        }
-        if (!next_ready && !(mbar_wait(&bars[B_PFULL + b], (J >> 1) & 1, p.err, ERR_TIMEOUT_MMA) &&
-                             mbar_wait(&bars[B_VFULL + b], (J >> 1) & 1, p.err, ERR_TIMEOUT_FULL))) {
-          ok = false;
+      for (int kk = 0; kk < 16; ++kk) s_mma(0, kk);
+      umma_pair_commit(&bars[B_SFULL], PF_PAIR);
+    }
+    bool next_ready = false;  // inputs of the next group already seen complete
+    for (int j = 0; ok && j < n_tiles; ++j) {
+      const int b = j & 1;
+      if (j + 1 < n_tiles) {
+        // S_{j+1}
+        if (!next_ready && !mbar_wait(&bars[B_KFULL + ((j + 1) & 1)], ((j + 1) >> 1) & 1, p.err, ERR_TIMEOUT_FULL))
           break;
-        }
         tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < 7; ++kk) pv_mma(J, i > 0, kk);
-        next_ready = i + 2 < n && k_ready(J + 2);
-        pv_mma(J, i > 0, 7);
-        umma_pair_commit(&bars[B_PVDONE + b], PF_PAIR);
+        for (int kk = 0; kk < 15; ++kk) s_mma(j + 1, kk);
+        next_ready = pv_ready(j);
+        s_mma(j + 1, 15);
+        umma_pair_commit(&bars[B_SFULL + ((j + 1) & 1)], PF_PAIR);
+      } else {
+        next_ready = false;
       }
-      J0 += n;
+      // P_j . V_j
+      if (!next_ready && !(mbar_wait(&bars[B_PFULL + b], (j >> 1) & 1, p.err, ERR_TIMEOUT_MMA) &&
+                           mbar_wait(&bars[B_VFULL + b], (j >> 1) & 1, p.err, ERR_TIMEOUT_FULL)))
+        break;
+      tc_fence_after();
+#pragma unroll
+      for (int kk = 0; kk < 7; ++kk) pv_mma(j, kk);
+      next_ready = j + 2 < n_tiles && k_ready(j + 2);
+      pv_mma(j, 7);
+      umma_pair_commit(&bars[B_PVDONE + b], PF_PAIR);
     }
     PT_FLUSH(0);
-  } else if (warp >= 4) {
+  }
+#if defined(LISA_PREFILL_TRACE) || defined(LISA_PREFILL_OBSERVE)
+  else if (warp == 3 && lane == 0 && blockIdx.x == 0) {
+    // observer: completion clocks of S_j (event 8) and P_j.V_j (event 9)
+    for (int j = 0; j < n_tiles && j < 64; ++j) {
+      mbar_wait(&bars[B_SFULL + (j & 1)], (j >> 1) & 1, nullptr, 0);
+      p.trace[2048 + 8 * 64 + j] = clock64();
+      if (j >= 1) {
+        mbar_wait(&bars[B_PVDONE + ((j - 1) & 1)], ((j - 1) >> 1) & 1, nullptr, 0);
+        p.trace[2048 + 9 * 64 + j - 1] = clock64();
+      }
+    }
+  }
+#endif
+  else if (warp >= 4) {
     // ---------------- softmax / correction / epilogue (warps 4..11) ----------------
     // Warp 4+w and warp 8+w share TMEM lanes 32w..32w+31 (one query row per
     // thread); each reads and exponentiates one half (64 keys) of a tile, and
@@ -485,247 +418,185 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
     const int half = (warp - 4) >> 2;
     const int row = wi * 32 + lane;  // row within the CTA's tile == TMEM lane
     const uint32_t lane_addr = tmem + ((uint32_t)(wi * 32) << 16);
-    int J0 = 0;
+    const uint32_t pos_row = p.base + (uint32_t)(r0 + row);
     bool ok = true;
-    for (int pi = 0; ok && pi < n_pieces; ++pi) {
-      const PfPiece pc = pieces[pi];
-      const uint32_t pos_row =
-          p.base + (uint32_t)((work.n_pairs - 1 - pc.unit / QH) * 2 * PF_BM + (int)rank * PF_BM + row);
-      const int n = pc.j1 - pc.j0;
-      const int j0 = pc.j0;
-      float mr = -INFINITY, l = 0.f;  // running max of the raw scores, this half's sum
-      for (int i = 0; i < n; ++i) {
-        const int J = J0 + i, b = J & 1;
-        PT(7);
-        if (!mbar_wait(&bars[B_SFULL + b], (J >> 1) & 1, p.err, ERR_TIMEOUT_MMA)) {
+    float mr = -INFINITY, l = 0.f;  // running max of the raw scores, this half's sum
+    for (int j = 0; j < n_tiles; ++j) {
+      const int b = j & 1;
+      PT(7);
+      if (!mbar_wait(&bars[B_SFULL + b], (j >> 1) & 1, p.err, ERR_TIMEOUT_MMA)) {
+        ok = false;
+        break;
+      }
+      PT(0);
+      if (lane == 0 && warp == 4) { PE(4, j); }
+      if (lane == 0 && j == 10) { PE(14, warp - 4); }
+      tc_fence_after();
+      uint32_t sa[32], sb[32];
+      const uint32_t scol = PF_TMEM_S + b * PF_BN + half * 64;
+      tmem_ld32(lane_addr + scol, sa);
+      tmem_ld32(lane_addr + scol + 32, sb);
+      tmem_wait_ld();
+      float x[64];  // raw scores Q.K (unscaled)
+#pragma unroll
+      for (int c = 0; c < 64; ++c) x[c] = __uint_as_float(c < 32 ? sa[c] : sb[c - 32]);
+      const uint32_t key0 = (uint32_t)j * PF_BN + half * 64;
+      if (key0 + 63 > pos_row) {  // diagonal tile: keys past this row's position
+#pragma unroll
+        for (int c = 0; c < 64; ++c)
+          if (key0 + c > pos_row) x[c] = -INFINITY;
+      }
+      float t8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        t8[i] = fmaxf(fmax3(fmax3(x[8 * i], x[8 * i + 1], x[8 * i + 2]), x[8 * i + 3], x[8 * i + 4]),
+                      fmax3(x[8 * i + 5], x[8 * i + 6], x[8 * i + 7]));
+      const float hmax = fmax3(fmax3(t8[0], t8[1], t8[2]), fmax3(t8[3], t8[4], t8[5]), fmaxf(t8[6], t8[7]));
+      xmax[(b * 2 + half) * PF_BM + row] = hmax;
+      // both halves have read this S tile (P overwrites its first 64 columns)
+      // and published their maxima
+      named_bar_sync(2 + wi, 64);
+      const float mnew = fmax3(mr, hmax, xmax[(b * 2 + (half ^ 1)) * PF_BM + row]);
+      // the running max moves only when it grows by more than 2^8 (in exp2 units)
+      const bool need = (mnew - mr) * kLog2Scale > PF_RESCALE_LOG2;  // also true for the first finite max
+      float alpha = 1.f;
+      if (need) {
+        alpha = fast_exp2((mr - mnew) * kLog2Scale);
+        mr = mnew;
+      }
+      // P = exp2(x * scale*log2e - m), rounded to bf16 and written over the S
+      // tile 16 keys at a time so the TMEM stores overlap the exponentials.
+      // 1 of every 8 key pairs is exponentiated on the FMA pipe, the rest on
+      // the SFU (measured on config 2: 1/8 and 2/8 are equal, 3/8 is 2 % and
+      // 4/8 6 % slower). The denominator sums the
+      // f32 values, as the reference's f32 softmax does.
+      const float2 cc = make_float2(kLog2Scale, kLog2Scale);
+      const float2 nm = make_float2(-mr * kLog2Scale, -mr * kLog2Scale);
+      float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t pk[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const float2 e = ffma2(make_float2(x[16 * q + 2 * c], x[16 * q + 2 * c + 1]), cc, nm);
+          const float2 pe = c < 1 ? exp2_poly2(e) : make_float2(fast_exp2(e.x), fast_exp2(e.y));
+          pk[c] = pack_bf16x2(pe.x, pe.y);
+          if (c & 1) acc1 = fadd2(acc1, pe);
+          else acc0 = fadd2(acc0, pe);
+        }
+        tmem_st8(lane_addr + PF_TMEM_S + b * PF_BN + half * 32 + q * 8, pk);
+      }
+      const float2 acc = fadd2(acc0, acc1);
+      l = l * alpha + (acc.x + acc.y);
+      PT(1);
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        // O must hold exactly tiles < j before it is rescaled
+        if (!mbar_wait(&bars[B_PVDONE + (b ^ 1)], ((j - 1) >> 1) & 1, p.err, ERR_TIMEOUT_MMA)) {
           ok = false;
           break;
         }
-        PT(0);
         tc_fence_after();
-        uint32_t sa[32], sb[32];
-        const uint32_t scol = PF_TMEM_S + b * PF_BN + half * 64;
-        tmem_ld32(lane_addr + scol, sa);
-        tmem_ld32(lane_addr + scol + 32, sb);
-        tmem_wait_ld();
-        float x[64];  // raw scores Q.K (unscaled)
-#pragma unroll
-        for (int c = 0; c < 64; ++c) x[c] = __uint_as_float(c < 32 ? sa[c] : sb[c - 32]);
-        const uint32_t key0 = (uint32_t)(j0 + i) * PF_BN + half * 64;
-        if (key0 + 63 > pos_row) {  // diagonal tile: keys past this row's position
-#pragma unroll
-          for (int c = 0; c < 64; ++c)
-            if (key0 + c > pos_row) x[c] = -INFINITY;
-        }
-        float t8[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q)
-          t8[q] = fmaxf(fmax3(fmax3(x[8 * q], x[8 * q + 1], x[8 * q + 2]), x[8 * q + 3], x[8 * q + 4]),
-                        fmax3(x[8 * q + 5], x[8 * q + 6], x[8 * q + 7]));
-        const float hmax = fmax3(fmax3(t8[0], t8[1], t8[2]), fmax3(t8[3], t8[4], t8[5]), fmaxf(t8[6], t8[7]));
-        xmax[(b * 2 + half) * PF_BM + row] = hmax;
-        // both halves have read this S tile (P overwrites its first 64 columns)
-        // and published their maxima
-        named_bar_sync(2 + wi, 64);
-        const float mnew = fmax3(mr, hmax, xmax[(b * 2 + (half ^ 1)) * PF_BM + row]);
-        // The running max moves only when it grows by more than 2^8 (in exp2
-        // units), or first becomes finite. A row whose keys in this piece are
-        // all masked so far keeps mr = -inf and gets P = 0.
-        const bool need = mnew != -INFINITY && (mr == -INFINITY || (mnew - mr) * kLog2Scale > PF_RESCALE_LOG2);
-        float alpha = 1.f;
-        if (need) {
-          alpha = fast_exp2((mr - mnew) * kLog2Scale);  // 0 when mr was -inf
-          mr = mnew;
-        }
-        // P = exp2(x * scale*log2e - m), rounded to bf16 and written over the S
-        // tile 16 keys at a time so the TMEM stores overlap the exponentials.
-        // 1 of every 8 key pairs is exponentiated on the FMA pipe, the rest on
-        // the SFU. The denominator sums the f32 values, as the reference's f32
-        // softmax does.
-        const float2 cc = make_float2(kLog2Scale, kLog2Scale);
-        const float moff = mr == -INFINITY ? 0.f : -mr * kLog2Scale;
-        const float2 nm = make_float2(moff, moff);
-        float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint32_t pk[8];
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            const float2 e = ffma2(make_float2(x[16 * q + 2 * c], x[16 * q + 2 * c + 1]), cc, nm);
-            const float2 pe = c < 1 ? exp2_poly2(e) : make_float2(fast_exp2(e.x), fast_exp2(e.y));
-            pk[c] = pack_bf16x2(pe.x, pe.y);
-            if (c & 1) acc1 = fadd2(acc1, pe);
-            else acc0 = fadd2(acc0, pe);
-          }
-          tmem_st8(lane_addr + PF_TMEM_S + b * PF_BN + half * 32 + q * 8, pk);
-        }
-        const float2 acc = fadd2(acc0, acc1);
-        l = l * alpha + (acc.x + acc.y);
-        PT(1);
-        if (i > 0 && __any_sync(0xffffffffu, need)) {
-          // O must hold exactly tiles < J of this piece before it is rescaled
-          if (!mbar_wait(&bars[B_PVDONE + (b ^ 1)], ((J - 1) >> 1) & 1, p.err, ERR_TIMEOUT_MMA)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-#pragma unroll 1
-          for (int c = 0; c < HD / 64; ++c) {
-            const uint32_t col = PF_TMEM_O + half * (HD / 2) + c * 32;
-            uint32_t ov[32];
-            tmem_ld32(lane_addr + col, ov);
-            tmem_wait_ld();
-#pragma unroll
-            for (int q = 0; q < 32; ++q) ov[q] = __float_as_uint(__uint_as_float(ov[q]) * alpha);
-            tmem_st32(lane_addr + col, ov);
-          }
-        }
-        PT(2);
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster_relaxed(lead_bar(B_PFULL + b));
-        PT(4);
-      }
-      if (!ok) break;
-      const int Jl = J0 + n - 1;
-      J0 += n;
-      ok = mbar_wait(&bars[B_PVDONE + (Jl & 1)], (Jl >> 1) & 1, p.err, ERR_TIMEOUT_MMA);
-      if (!ok) break;
-      // Row denominators: this half's plus the other half's.
-      xsum[half * PF_BM + row] = l;
-      named_bar_sync(2 + wi, 64);
-      const float l_row = xsum[row] + xsum[PF_BM + row];
-      named_bar_sync(2 + wi, 64);  // both halves have read xsum before the next piece writes it
-      tc_fence_after();
-      const PfPiece pe = pieces[pi];
-      float den = l_row;
-      if (!(pe.first && pe.last)) {
-        // ---- a unit split over clusters c_first .. c_last. Every segment
-        // leaves its partial (unnormalised O of this CTA's rows, max, row
-        // sum); the last one to finish (counted per unit and rank) merges all
-        // of them in cluster order, so the result does not depend on which
-        // cluster arrives last. Nobody waits, so the clusters need not be
-        // resident at the same time. ----
-        const int u_off = work.unit_off(pe.unit), u_end = u_off + work.unit_tiles(pe.unit);
-        int c_first = cl, c_last = cl;
-        while (c_first > 0 && work.range_start(c_first) > u_off) --c_first;
-        while (c_last + 1 < work.clusters && work.range_start(c_last + 1) < u_end) ++c_last;
-        // a segment's slot: its cluster's first piece (which 0) or, for the
-        // cluster whose range starts before the unit, its last piece (1)
-        auto slot_ptr = [&](int c) -> float* {
-          const int which = work.range_start(c) < u_off ? 1 : 0;
-          return p.part + ((((size_t)c * 2 + which) * 2 + rank) * PF_BM + row) * PF_PART_STRIDE;
-        };
-        float* dst = slot_ptr(cl);
 #pragma unroll 1
         for (int c = 0; c < HD / 64; ++c) {
-          const int col = half * (HD / 2) + c * 32;
+          const uint32_t col = PF_TMEM_O + half * (HD / 2) + c * 32;
           uint32_t ov[32];
-          tmem_ld32(lane_addr + PF_TMEM_O + col, ov);
+          tmem_ld32(lane_addr + col, ov);
           tmem_wait_ld();
 #pragma unroll
-          for (int q = 0; q < 8; ++q)
-            __stcg(reinterpret_cast<uint4*>(dst + col + 4 * q),
-                   make_uint4(ov[4 * q], ov[4 * q + 1], ov[4 * q + 2], ov[4 * q + 3]));
-        }
-        if (half == 0) __stcg(reinterpret_cast<float2*>(dst + HD), make_float2(mr, l_row));
-        __threadfence();
-        named_bar_sync(6, 256);  // the whole partial of this CTA is written
-        if (threadIdx.x == 128) {
-          uint32_t* cnt = p.ready + pe.unit * 2 + rank;
-          const uint32_t before = atomicAdd(cnt, 1u);
-          const bool last = before == (uint32_t)(c_last - c_first);
-          if (last) *cnt = 0u;  // every segment has arrived: ready for the next call
-          __threadfence();
-          *seg_ok = last ? 1u : 0u;
-        }
-        named_bar_sync(6, 256);
-        const bool merge = *seg_ok != 0u;
-        named_bar_sync(6, 256);
-        if (!merge) {
-          tc_fence_before();
-          continue;
-        }
-        // O = sum_s O_s * w_s, den = sum_s l_s * w_s, w_s = 2^((m_s - m_all) c)
-        float mall = -INFINITY;
-        for (int c = c_first; c <= c_last; ++c) mall = fmaxf(mall, __ldcg(slot_ptr(c) + HD));
-        den = 0.f;
-        for (int c = c_first; c <= c_last; ++c) {
-          const float2 ml = __ldcg(reinterpret_cast<const float2*>(slot_ptr(c) + HD));
-          den += ml.y * (ml.x == -INFINITY ? 0.f : fast_exp2((ml.x - mall) * kLog2Scale));
-        }
-#pragma unroll 1
-        for (int c = 0; c < HD / 64; ++c) {
-          const int col = half * (HD / 2) + c * 32;
-          uint32_t ov[32];
-#pragma unroll
-          for (int q = 0; q < 32; ++q) ov[q] = 0u;
-          for (int cc = c_first; cc <= c_last; ++cc) {
-            const float* sp = slot_ptr(cc);
-            const float mk = __ldcg(sp + HD);
-            const float wk = mk == -INFINITY ? 0.f : fast_exp2((mk - mall) * kLog2Scale);
-            const float4* s4 = reinterpret_cast<const float4*>(sp + col);
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              const float4 v4 = __ldcg(s4 + q);
-              ov[4 * q] = __float_as_uint(fmaf(v4.x, wk, __uint_as_float(ov[4 * q])));
-              ov[4 * q + 1] = __float_as_uint(fmaf(v4.y, wk, __uint_as_float(ov[4 * q + 1])));
-              ov[4 * q + 2] = __float_as_uint(fmaf(v4.z, wk, __uint_as_float(ov[4 * q + 2])));
-              ov[4 * q + 3] = __float_as_uint(fmaf(v4.w, wk, __uint_as_float(ov[4 * q + 3])));
-            }
-          }
-          tmem_st32(lane_addr + PF_TMEM_O + col, ov);
-        }
-        tmem_wait_st();
-      }
-      // ---- gated output of the unit's rows: O / den * sigmoid(gate). Every
-      // lane takes part in the TMEM loads (warp-collective); rows past the
-      // chunk only skip their gate loads and stores. ----
-      {
-        const int h = pe.unit % QH;
-        const int r = (work.n_pairs - 1 - pe.unit / QH) * 2 * PF_BM + (int)rank * PF_BM + row;
-        const bool valid = r < p.rows;
-        const float inv_l = 1.0f / den;
-        const size_t gbase = (size_t)r * QROW + (size_t)h * 512 + 256 + half * 128;
-        uint16_t* out = p.gated_out + (size_t)r * OROW + (size_t)h * HD + half * (HD / 2);
-        uint4 g4[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          g4[q] = valid ? load8_bf16(p.q_gate, gbase + 8 * q, p.in_bf16) : make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-        for (int c = 0; c < HD / 64; ++c) {
-          const int col = half * (HD / 2) + c * 32;
-          uint32_t ov[32];
-          tmem_ld32(lane_addr + PF_TMEM_O + col, ov);
-          uint4 gn[4];  // the next 32 dims' gate, in flight during this pass
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            gn[q] = (valid && c + 1 < HD / 64) ? load8_bf16(p.q_gate, gbase + 32 * (c + 1) + 8 * q, p.in_bf16)
-                                               : make_uint4(0u, 0u, 0u, 0u);
-          tmem_wait_ld();
-          uint32_t outw[16];
-#pragma unroll
-          for (int q = 0; q < 16; ++q) {
-            const uint32_t gw = (&g4[q >> 2].x)[q & 3];
-            const float2 g2 = unpack_bf16x2(gw);
-            outw[q] = pack_bf16x2(__uint_as_float(ov[2 * q]) * inv_l * fast_sigmoid(g2.x),
-                                  __uint_as_float(ov[2 * q + 1]) * inv_l * fast_sigmoid(g2.y));
-          }
-          if (valid) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-              *reinterpret_cast<uint4*>(out + c * 32 + 8 * q) =
-                  make_uint4(outw[4 * q], outw[4 * q + 1], outw[4 * q + 2], outw[4 * q + 3]);
-          }
-#pragma unroll
-          for (int q = 0; q < 4; ++q) g4[q] = gn[q];
+          for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+          tmem_st32(lane_addr + col, ov);
         }
       }
+      PT(2);
+      tmem_wait_st();
       tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster_relaxed(lead_bar(B_PFULL + b));
+      if (lane == 0 && warp == 4) { PE(5, j); }
+      if (lane == 0 && warp == 8) { PE(6, j); }
+      if (lane == 0 && j == 10) { PE(13, warp - 4); }
+      PT(4);
+    }
+#ifdef LISA_PREFILL_TRACE
+    if (threadIdx.x == 128) p.trace[64 + blockIdx.x * 8 + 3] = global_timer_ns();
+#endif
+    // Gate values of this row and half. bf16 inputs: the K producer has
+    // brought this CTA's gate tile into the K ring ([group][row][64],
+    // 128-byte swizzle) once the last S was computed. f32 inputs: loaded
+    // here, rounded to bf16 as the reference does.
+    const int r = r0 + row;
+    uint32_t gpk[64];
+    if (!p.in_bf16 && ok && r < p.rows) {
+      const size_t gbase = (size_t)r * QROW + (size_t)h * 512 + 256 + half * 128;
+#pragma unroll
+      for (int g8 = 0; g8 < 16; ++g8) {
+        float gv[8];
+        load8_in(p.q_gate, gbase + g8 * 8, 0, gv);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) gpk[g8 * 4 + i] = pack_bf16x2(gv[2 * i], gv[2 * i + 1]);
+      }
+    }
+    const int last = n_tiles - 1;
+    ok = ok && mbar_wait(&bars[B_PVDONE + (last & 1)], (last >> 1) & 1, p.err, ERR_TIMEOUT_MMA);
+#ifdef LISA_PREFILL_TRACE
+    if (threadIdx.x == 128) p.trace[64 + blockIdx.x * 8 + 2] = global_timer_ns();
+#endif
+    // Sum the two halves' denominators (half 0 + half 1).
+    xsum[half * PF_BM + row] = l;
+    named_bar_sync(2 + wi, 64);
+    const float l_row = xsum[row] + xsum[PF_BM + row];
+    if (p.in_bf16) ok = ok && mbar_wait(&bars[B_G], 0, p.err, ERR_TIMEOUT_FULL);
+    // gated rows staged in the (now idle) V ring as [group][row][64] with the
+    // 128-byte swizzle, then written by one TMA store (rows >= p.rows clipped)
+    uint8_t* stage = smem + PF_OFF_V;
+    const uint8_t* gtile = smem + PF_OFF_K;
+    if (ok) {
+      tc_fence_after();
+      const float inv_l = 1.0f / l_row;
+#pragma unroll
+      for (int c = 0; c < HD / 64; ++c) {
+        const int col = half * (HD / 2) + c * 32;  // first of this pass's 32 dims
+        const int grp = col >> 6, ch0 = (col & 63) >> 3;
+        uint32_t ov[32];
+        tmem_ld32(lane_addr + PF_TMEM_O + col, ov);
+        uint32_t gw[16];
+        if (p.in_bf16) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint4 g4 = *reinterpret_cast<const uint4*>(gtile + grp * (PF_BM * 128) + row * 128 +
+                                                             (((ch0 + i) ^ (row & 7)) << 4));
+            gw[4 * i] = g4.x; gw[4 * i + 1] = g4.y; gw[4 * i + 2] = g4.z; gw[4 * i + 3] = g4.w;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) gw[i] = gpk[c * 16 + i];
+        }
+        tmem_wait_ld();
+        uint32_t outw[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float2 g2 = unpack_bf16x2(gw[i]);
+          outw[i] = pack_bf16x2(__uint_as_float(ov[2 * i]) * inv_l * fast_sigmoid(g2.x),
+                                __uint_as_float(ov[2 * i + 1]) * inv_l * fast_sigmoid(g2.y));
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          *reinterpret_cast<uint4*>(stage + grp * (PF_BM * 128) + row * 128 + (((ch0 + i) ^ (row & 7)) << 4)) =
+              make_uint4(outw[4 * i], outw[4 * i + 1], outw[4 * i + 2], outw[4 * i + 3]);
+      }
+    }
+    fence_proxy_async_smem();
+    named_bar_sync(6, 256);  // the staged tile is complete
+    if (ok && threadIdx.x == 128) {
+      tma_store_4d(&to, stage, 0, r0, 0, h);
+      bulk_commit_group();
+      bulk_wait_read();  // the staging must stay until the store has read it
     }
     PT(5);
     if (warp == 4) { PT_FLUSH(1); }
+#ifdef LISA_PREFILL_TRACE
+    if (threadIdx.x == 128) p.trace[64 + blockIdx.x * 8 + 4] = global_timer_ns();
+#endif
   }
   // Both CTAs are done with TMEM and with each other's barriers before either
   // frees its columns or exits.
@@ -738,52 +609,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
   }
 }
 
-namespace {
-constexpr size_t PF_QWS_BYTES = (size_t)QH * PF_MAX_ROWS * HD * sizeof(uint16_t);
-constexpr size_t PF_PART_BYTES = (size_t)PF_MAX_CLUSTERS * 2 * 2 * PF_BM * PF_PART_STRIDE * sizeof(float);
-}  // namespace
-
-size_t prefill_workspace_bytes() { return PF_QWS_BYTES + PF_PART_BYTES + PF_MAX_CLUSTERS * 2 * sizeof(uint32_t); }
-
-void prefill_workspace_layout(void* ws, uint16_t** q_ws, float** part, uint32_t** ready) {
-  uint8_t* b = static_cast<uint8_t*>(ws);
-  *q_ws = reinterpret_cast<uint16_t*>(b);
-  *part = reinterpret_cast<float*>(b + PF_QWS_BYTES);
-  *ready = reinterpret_cast<uint32_t*>(b + PF_QWS_BYTES + PF_PART_BYTES);
-}
-
-namespace {
-// cudaOccupancyMaxActiveClusters for the attention kernel, per device.
-int max_resident_clusters(const cudaLaunchConfig_t& base_cfg) {
-  static std::mutex mu;
-  static int cached[64] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 1;
-  std::lock_guard<std::mutex> lock(mu);
-  if (!cached[dev]) {
-    cudaLaunchConfig_t cfg = base_cfg;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    cfg.gridDim = dim3(2 * PF_MAX_CLUSTERS);
-    cfg.blockDim = dim3(PF_THREADS);
-    cfg.dynamicSmemBytes = PF_SMEM_BYTES;
-    int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, prefill_attn_kernel, &cfg) != cudaSuccess || n < 1) {
-      cudaGetLastError();
-      n = 1;
-    }
-    cached[dev] = n;
-  }
-  return cached[dev];
-}
-}  // namespace
+size_t prefill_workspace_bytes() { return (size_t)QH * PF_MAX_ROWS * HD * sizeof(uint16_t); }
 
 cudaError_t launch_prefill(const PrefillParams& p_in, int num_sms, cudaStream_t stream) {
+  (void)num_sms;
   PrefillParams p = p_in;
   host_inv_freq(p.inv_freq);
   cudaLaunchAttribute attr[1];
@@ -800,46 +629,20 @@ cudaError_t launch_prefill(const PrefillParams& p_in, int num_sms, cudaStream_t 
   static SmemAttr attr_once;  // the attribute is per kernel and per device
   e = attr_once.ensure(prefill_attn_kernel, PF_SMEM_BYTES);
   if (e != cudaSuccess) return e;
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk, tv, tg = {}, to;
   const uint32_t kv_rows = p.base + (uint32_t)p.rows;
   if (lisa_encode_group_map(&tq, p.q_ws, PF_MAX_ROWS, PF_MAX_ROWS, QH, PF_BM, 4) != 0 ||
       lisa_encode_group_map(&tk, p.k_cache, kv_rows, p.capacity, KVH, PF_BN / 2, 4) != 0 ||
-      lisa_encode_group_map(&tv, p.v_cache, kv_rows, p.capacity, KVH, PF_BN, 2) != 0)
+      lisa_encode_group_map(&tv, p.v_cache, kv_rows, p.capacity, KVH, PF_BN, 2) != 0 ||
+      lisa_encode_rows_map(&to, p.gated_out, (uint32_t)p.rows, OROW, 4, QH, HD, PF_BM) != 0 ||
+      (p.in_bf16 && lisa_encode_rows_map(&tg, p.q_gate, (uint32_t)p.rows, QROW, 8, QH, 512, PF_BM) != 0))
     return cudaErrorInvalidValue;
-  // Work split: one cluster per unit, or (stream-K) every cluster slot of the
-  // GPU taking an equal share of all units' key tiles when that shortens the
-  // longest cluster by more than the cost of splitting (about two tiles: the
-  // query reload, the partial written and merged).
   const int n_qt = (p.rows + PF_BM - 1) / PF_BM;
   const int n_pairs = (n_qt + 1) / 2;
-  const int units = n_pairs * QH;
-  int total = 0, longest = 0, shortest = 1 << 30;
-  for (int qp = 0; qp < n_pairs; ++qp) {
-    const int end = std::min(qp * 2 * PF_BM + 2 * PF_BM, p.rows);
-    const int n = (int)((p.base + (uint32_t)end + PF_BN - 1) / PF_BN);
-    total += QH * n;
-    longest = std::max(longest, n);
-    shortest = std::min(shortest, n);
-  }
-  // Stream-K clusters wait for one another's partials, so all of them must be
-  // resident at once: at most the number of 2-CTA clusters of this kernel the
-  // device can hold (queried once per device).
-  const int slots = std::min(PF_MAX_CLUSTERS, std::max(1, std::min(num_sms / 2, max_resident_clusters(cfg))));
-  const int share = (total + slots - 1) / slots;
-  p.total_tiles = total;
-  const int mode = current_prefill_split();
-  const bool fits = (share + shortest - 1) / shortest + 2 <= PF_MAX_PIECES;  // pieces per cluster
-  if (units < slots && fits && (mode == 2 || (mode == 0 && share + 2 < longest))) {
-    p.streamk = 1;
-    p.clusters = slots;
-  } else {
-    p.streamk = 0;
-    p.clusters = units;
-  }
-  cfg.gridDim = dim3(p.clusters * 2);
+  cfg.gridDim = dim3(n_pairs * QH * 2);
   cfg.blockDim = dim3(PF_THREADS);
   cfg.dynamicSmemBytes = PF_SMEM_BYTES;
-  return cudaLaunchKernelEx(&cfg, prefill_attn_kernel, tq, tk, tv, p);
+  return cudaLaunchKernelEx(&cfg, prefill_attn_kernel, tq, tk, tv, tg, to, p);
 }
 
 }  // namespace lisa

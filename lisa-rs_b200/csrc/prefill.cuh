@@ -18,8 +18,6 @@ int lisa_encode_rows_map(CUtensorMap* map, const void* base, uint32_t rows, uint
 namespace lisa {
 
 constexpr int PF_MAX_ROWS = 512;
-constexpr int PF_PART_STRIDE = 260;   // floats per row of a split partial: O[256], max, sum, 2 pad
-constexpr int PF_MAX_CLUSTERS = 96;  // stream-K clusters (one per 2 SMs)
 
 struct PrefillParams {
   const void* q_gate;  // [rows][24][512]
@@ -37,29 +35,14 @@ struct PrefillParams {
   uint16_t* q_ws;     // workspace: normalised query, bf16 [24 heads][512 rows][256]
   uint16_t* gated_out;  // [rows][6144]
   int* err;
-  // Work split of the attention kernel. A unit is (query-row pair of 256
-  // rows, head); its key tiles are numbered 0 .. tiles-1; units are ordered
-  // heaviest first and their tiles concatenated into one list of
-  // total_tiles. streamk = 0: cluster c runs unit c. streamk = 1: cluster c
-  // runs tiles [c*total/clusters, (c+1)*total/clusters) of the list; every
-  // cluster holding part of a split unit leaves a partial and the last one
-  // to finish merges them.
-  int streamk;
-  int clusters;
-  int total_tiles;
-  float* part;       // [clusters][2: first / last piece][2 ranks][128 rows][PF_PART_STRIDE]: O, max, sum
-  uint32_t* ready;   // [units][2 ranks]: segments of a split unit that have finished (reset by the last)
   float inv_freq[32];  // filled by launch_prefill
 #if defined(LISA_PREFILL_TRACE) || defined(LISA_PREFILL_OBSERVE)
   unsigned long long* trace;  // debug builds only
 #endif
 };
 
-// Bytes of device workspace launch_prefill needs: the query workspace, the
-// split partials and their ready flags (zero-filled by the owner).
+// Bytes of device workspace launch_prefill needs.
 size_t prefill_workspace_bytes();
-// Carves the workspace into q_ws / part / ready.
-void prefill_workspace_layout(void* ws, uint16_t** q_ws, float** part, uint32_t** ready);
 
 // Prologue (q norm/RoPE into q_ws, K/V append) then the tcgen05 attention.
 cudaError_t launch_prefill(const PrefillParams& p, int num_sms, cudaStream_t stream);

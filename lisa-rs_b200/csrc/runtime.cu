@@ -89,10 +89,8 @@ namespace lisa {
 namespace {
 std::atomic<uint64_t> g_fault_limit_ns{0};
 std::atomic<int> g_fault_withhold{0};
-std::atomic<int> g_prefill_split{0};
 }  // namespace
 
-int current_prefill_split() { return g_prefill_split.load(std::memory_order_relaxed); }
 
 WaitFault current_wait_fault() {
   return WaitFault{g_fault_limit_ns.load(std::memory_order_relaxed), g_fault_withhold.load(std::memory_order_relaxed)};
@@ -296,7 +294,7 @@ int lisa_attn_prefill_chunk(lisa_attn_ctx* c, int layer, uint32_t base, int rows
   p.capacity = c->capacity;
   p.base = base;
   p.rows = rows;
-  prefill_workspace_layout(c->prefill_ws, &p.q_ws, &p.part, &p.ready);
+  p.q_ws = reinterpret_cast<uint16_t*>(c->prefill_ws);
   p.gated_out = gated_out;
   p.err = c->err;
   return cuda_status(launch_prefill(p, c->num_sms, (cudaStream_t)stream));
@@ -449,12 +447,6 @@ int lisa_attn_window_check_device_error(void* workspace, void* stream) {
     return LISA_ECUDA;
   if (h && cudaMemsetAsync(workspace, 0, sizeof(int), st) != cudaSuccess) return LISA_ECUDA;
   return h ? LISA_ETIMEOUT : LISA_OK;
-}
-
-int lisa_attn_debug_prefill_split(int mode) {
-  if (mode < 0 || mode > 2) return LISA_EINVAL;
-  g_prefill_split.store(mode, std::memory_order_relaxed);
-  return LISA_OK;
 }
 
 int lisa_attn_debug_wait_fault(uint32_t wait_limit_us, int withhold_loads) {

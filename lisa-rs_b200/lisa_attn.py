@@ -71,7 +71,6 @@ SIGNATURES = {
     "lisa_attn_decode_noalloc": (_i32, [_P, _P, _u32, _u32, _i32, _i32, _P, _P, _P, _P, _P, _f32, _P, _P]),
     "lisa_attn_noalloc_check_device_error": (_i32, []),
     "lisa_attn_debug_wait_fault": (_i32, [_u32, _i32]),
-    "lisa_attn_debug_prefill_split": (_i32, [_i32]),
     "lisa_attn_dev_count": (_i32, [ctypes.POINTER(_i32)]),
     "lisa_attn_dev_info": (_i32, [_i32, ctypes.c_char_p, _sz, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(_i32)]),
     "lisa_attn_dev_select": (_i32, [_i32]),
