@@ -295,6 +295,32 @@ int lisa_attn_noalloc_check_device_error(void);
  * withhold_loads without a limit or a limit above 10 s. */
 int lisa_attn_debug_wait_fault(uint32_t wait_limit_us, int withhold_loads);
 
+/* ---- affine-u4 projections (QMV) --------------------------------------------
+ * The quantised matrix-vector products around the attention layer for the
+ * decode (rows = 1) and verify (rows = 3) shapes: q4_qmv_fast / fused2/3/4
+ * (src/kernels/shaders/qmv.metal:1-133) as dispatched by encode_qmv_fused
+ * (src/model/runner.rs:1134-1192). Weights are MLX affine 4-bit, group size
+ * 64: packed [n][k/8] uint32 (element j in bits 4*(j%8) of word j/8), scales
+ * and biases bf16 [n][k/64], w = q * scale + bias. x is bf16 [rows][k]; each
+ * projection writes f32 out [rows][n]:
+ *   out[m][r] = sum_j x[m][j] * (q[r][j] * scale[r][j/64] + bias[r][j/64]).
+ * One launch serves up to LISA_ATTN_QMV_MAX_PROJ projections of the same x
+ * (q_proj + k_proj + v_proj as fused3 does; their outputs are what
+ * lisa_attn_decode takes as q_gate, k, v with LISA_DTYPE_F32). k must be a
+ * multiple of 64 in 64..LISA_ATTN_QMV_MAX_K, packed 16-byte aligned;
+ * LISA_EINVAL otherwise. */
+#define LISA_ATTN_QMV_MAX_PROJ 4
+#define LISA_ATTN_QMV_MAX_ROWS 4
+#define LISA_ATTN_QMV_MAX_K 8192
+typedef struct {
+  const void* packed;     /* [n][k/8] uint32 */
+  const uint16_t* scales; /* [n][k/64] bf16 */
+  const uint16_t* biases; /* [n][k/64] bf16 */
+  float* out;             /* [rows][n] f32 */
+  int n;
+} lisa_attn_q4_proj;
+int lisa_attn_qmv_u4(int n_proj, const lisa_attn_q4_proj* projs, int rows, int k, const uint16_t* x, void* stream);
+
 /* ---- device bridge ----------------------------------------------------------
  * Thin wrappers over the CUDA runtime so a host in another language drives the
  * entry points above with this library alone. They replace lisa-rs's Metal

@@ -71,6 +71,7 @@ SIGNATURES = {
     "lisa_attn_decode_noalloc": (_i32, [_P, _P, _u32, _u32, _i32, _i32, _P, _P, _P, _P, _P, _f32, _P, _P]),
     "lisa_attn_noalloc_check_device_error": (_i32, []),
     "lisa_attn_debug_wait_fault": (_i32, [_u32, _i32]),
+    "lisa_attn_qmv_u4": (_i32, [_i32, _P, _i32, _i32, _P, _P]),
     "lisa_attn_dev_count": (_i32, [ctypes.POINTER(_i32)]),
     "lisa_attn_dev_info": (_i32, [_i32, ctypes.c_char_p, _sz, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(_i32)]),
     "lisa_attn_dev_select": (_i32, [_i32]),
@@ -432,3 +433,27 @@ class BatchDecoder:
             self.close()
         except Exception:
             pass
+
+
+# ---- affine-u4 projections (QMV) ----------------------------------------------
+
+class Q4Proj(ctypes.Structure):
+    """lisa_attn_q4_proj: one affine-u4 projection (device pointers) and its output."""
+    _fields_ = [("packed", _P), ("scales", _P), ("biases", _P), ("out", _P), ("n", _i32)]
+
+
+def qmv_u4(x, projections, out=None, stream=None):
+    """x bf16 [rows, k]; projections: list of (packed uint32 [n, k/8] (int32
+    tensor), scales bf16 [n, k/64], biases bf16 [n, k/64]). Returns the f32
+    outputs [rows, n] (one per projection), computed by one launch of
+    lisa_attn_qmv_u4 (the fused q/k/v QMV of the decode step)."""
+    import torch
+
+    rows, k = x.shape
+    outs = out or [torch.empty((rows, pk.shape[0]), dtype=torch.float32, device=x.device)
+                   for pk, _, _ in projections]
+    arr = (Q4Proj * len(projections))(*[
+        Q4Proj(_ptr(pk), _ptr(sc), _ptr(bi), _ptr(o), pk.shape[0]) for (pk, sc, bi), o in zip(projections, outs)])
+    _check("lisa_attn_qmv_u4",
+           load_library().lisa_attn_qmv_u4(len(projections), arr, rows, k, _ptr(x.contiguous()), _stream_ptr(stream)))
+    return outs

@@ -143,3 +143,26 @@ def num_threads() -> int:
 
 def set_num_threads(n: int) -> None:
     lib().orc_set_num_threads(n)
+
+
+# ---- affine-u4 QMV (numpy) ---------------------------------------------------
+
+def q4_qmv(x_bits, packed, scale_bits, bias_bits):
+    """out[m][n] = sum_k bf16(x[m][k]) * (q[n][k] * scale[n][k/64] + bias[n][k/64]),
+    the arithmetic of q4_qmv_fast_impl (src/kernels/shaders/qmv.metal:1-77):
+    nibble k%8 of word k/8 (low first), group size 64, bf16 scales / biases.
+    Evaluated in float64 (the kernel and the reference sum in f32 in their own
+    orders); returns float32 [M, N]."""
+    x_bits = np.asarray(x_bits, np.uint16)
+    packed = np.asarray(packed, np.uint32)
+    m_rows, k = x_bits.shape
+    n = packed.shape[0]
+    q = ((packed[:, :, None] >> (4 * np.arange(8, dtype=np.uint32))) & 0xF).reshape(n, k).astype(np.float64)
+    s = bf16_to_f32(np.asarray(scale_bits, np.uint16).reshape(n, k // 64)).astype(np.float64)
+    b = bf16_to_f32(np.asarray(bias_bits, np.uint16).reshape(n, k // 64)).astype(np.float64)
+    x = bf16_to_f32(x_bits).astype(np.float64)
+    # sum_k x*(q*s+b) = sum_g s_g * sum_{k in g} x q + b_g * sum_{k in g} x
+    xq = (x[:, None, :] * q[None, :, :]).reshape(m_rows, n, k // 64, 64).sum(-1)
+    xs = x.reshape(m_rows, k // 64, 64).sum(-1)
+    out = (xq * s[None]).sum(-1) + (xs[:, None, :] * b[None]).sum(-1)
+    return out.astype(np.float32)

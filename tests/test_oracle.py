@@ -111,3 +111,12 @@ def test_rope_position_zero_is_identity_rotation():
     want = x * inv * O.bf16_to_f32(qn)[None]
     assert np.abs(O.bf16_to_f32(query[0]) - want).max() < 2e-2
     assert np.array_equal(gate[0], O.bf16_to_f32(O.f32_to_bf16(q[0].reshape(QH, 512)[:, HD:])))
+
+
+def test_qmv_oracle_matches_reference_kat():
+    """tests/qmv.rs:5-220: the affine-u4 QMV known-answer cases (M=1 and the
+    3-row wide variant, N=19 with a tail, K=128) at the reference tolerance."""
+    g = np.load(os.path.join(os.path.dirname(GOLD), "qmv_reference_tests.npz"))
+    for pre in ("m1", "m3"):
+        got = O.q4_qmv(g[pre + "_x"], g[pre + "_packed"], g[pre + "_scales"], g[pre + "_biases"])
+        assert np.abs(got - g[pre + "_expected"]).max() < 2e-4, pre
