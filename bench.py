@@ -499,6 +499,47 @@ def bench_batched(args, rank, world, local):
             "launches": 3 * LAYERS}
 
 
+def bench_qmv(args, world):
+    """The fused q/k/v affine-u4 QMV of a decode step (lisa_attn_qmv_u4, M=1,
+    hidden 5120 -> 12288 + 1024 + 1024 rows): four layers' weight sets are
+    cycled (4 x 41 MB, larger than L2) so every launch streams its weights
+    from HBM; one CUDA graph of 16 launches per step."""
+    import torch
+
+    import lisa_attn
+
+    k = 5120
+    ns = (QROW, KROW, KROW)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(0x5EED + 11)
+    sets = []
+    for _ in range(4):
+        projs = []
+        for n in ns:
+            pk = torch.randint(-2 ** 31, 2 ** 31 - 1, (n, k // 8), generator=gen, device="cuda", dtype=torch.int32)
+            sc = (0.01 + 0.01 * torch.rand((n, k // 64), generator=gen, device="cuda")).to(torch.bfloat16)
+            bi = (-0.08 * torch.rand((n, k // 64), generator=gen, device="cuda")).to(torch.bfloat16)
+            projs.append((pk, sc, bi))
+        sets.append(projs)
+    x = torch.randn((1, k), generator=gen, device="cuda").to(torch.bfloat16)
+    outs = [torch.empty((1, n), dtype=torch.float32, device="cuda") for n in ns]
+    stream = torch.cuda.current_stream()
+    for i in range(4):
+        lisa_attn.qmv_u4(x, sets[i], outs, stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    cs = torch.cuda.Stream()
+    with torch.cuda.stream(cs):
+        with torch.cuda.graph(graph, stream=cs):
+            for i in range(16):
+                lisa_attn.qmv_u4(x, sets[i % 4], outs, cs)
+    torch.cuda.synchronize()
+    ms = timed(graph.replay, args.steps, args.warmup, world, stream)
+    us = ms * 1000.0 / args.steps / 16
+    nbytes = sum(n * (k // 2 + (k // 64) * 4) for n in ns) + k * 2 + sum(ns) * 4
+    return us, nbytes
+
+
 def emit(line: dict) -> None:
     print(json.dumps(line), flush=True)
 
@@ -601,6 +642,8 @@ def main():
     torch.cuda.empty_cache()
     pf_ms, pf_ms_eager = bench_prefill(args, world)
     torch.cuda.empty_cache()
+    qmv_us, qmv_bytes = bench_qmv(args, world)
+    torch.cuda.empty_cache()
     blocks = {}
     if not args.decode_only:
         rb = bench_batched(args, rank, world, local)
@@ -661,6 +704,12 @@ def main():
                                  "kernel": "prefill_prologue_kernel + prefill_attn_kernel, 8 chunk calls"},
                     "gpu_launches_per_step": 2 * (PREFILL_TOKENS // PREFILL_CHUNK)},
     }
+    qmv_gbs = qmv_bytes / (qmv_us * 1e-6) / 1e9
+    line["qmv"] = {"workload": "fused q/k/v affine-u4 QMV of one decode step (lisa_attn_qmv_u4, M=1, 5120 -> "
+                               "12288+1024+1024), 4 weight sets cycled (164 MB > L2), 16 launches per CUDA graph",
+                   "us_per_launch": round(qmv_us, 3), "algorithmic_bytes": qmv_bytes,
+                   "roofline": {"bound": "hbm", "achieved": round(qmv_gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                                "frac": round(qmv_gbs / pk["hbm_gbs"], 4), "traffic": None}}
     line.update(blocks)
     emit(line)
     if world > 1:

@@ -321,6 +321,38 @@ typedef struct {
 } lisa_attn_q4_proj;
 int lisa_attn_qmv_u4(int n_proj, const lisa_attn_q4_proj* projs, int rows, int k, const uint16_t* x, void* stream);
 
+/* ---- safetensors shards (weights) ------------------------------------------
+ * Host-side reader of the checkpoint container (src/format/safetensor.rs:
+ * 1-91): [u64 LE header length][JSON header][tensor bytes], data_offsets
+ * relative to the end of the header, top-level keys starting with "__"
+ * skipped. The file is memory-mapped read-only. dtype codes follow the
+ * reference's names (src/format/dtype.rs:17-31): LISA_ST_* below. Unlike the
+ * reference (which panics), a malformed header, an unknown dtype, or a byte
+ * range outside the file or not matching the shape gives LISA_EINVAL from
+ * lisa_attn_st_open. lisa_attn_st_find returns the index or LISA_EINVAL.
+ * lisa_attn_st_upload copies one tensor to device memory (synchronous on
+ * `stream`). */
+#define LISA_ST_BOOL 0
+#define LISA_ST_U8 1
+#define LISA_ST_U16 2
+#define LISA_ST_I16 3
+#define LISA_ST_F16 4
+#define LISA_ST_BF16 5
+#define LISA_ST_U32 6
+#define LISA_ST_I32 7
+#define LISA_ST_F32 8
+#define LISA_ST_U64 9
+#define LISA_ST_F64 10
+typedef struct lisa_attn_shard lisa_attn_shard;
+int lisa_attn_st_open(const char* path, lisa_attn_shard** out);
+int lisa_attn_st_close(lisa_attn_shard* s);
+int lisa_attn_st_count(const lisa_attn_shard* s);
+int lisa_attn_st_find(const lisa_attn_shard* s, const char* name);
+int lisa_attn_st_info(const lisa_attn_shard* s, int index, char* name, size_t name_bytes, int* dtype,
+                      uint64_t* shape, int max_dims, int* ndim, uint64_t* data_offset, uint64_t* nbytes);
+int lisa_attn_st_host_ptr(const lisa_attn_shard* s, int index, const void** ptr);
+int lisa_attn_st_upload(const lisa_attn_shard* s, int index, void* dst, size_t dst_bytes, void* stream);
+
 /* ---- device bridge ----------------------------------------------------------
  * Thin wrappers over the CUDA runtime so a host in another language drives the
  * entry points above with this library alone. They replace lisa-rs's Metal

@@ -72,6 +72,15 @@ SIGNATURES = {
     "lisa_attn_noalloc_check_device_error": (_i32, []),
     "lisa_attn_debug_wait_fault": (_i32, [_u32, _i32]),
     "lisa_attn_qmv_u4": (_i32, [_i32, _P, _i32, _i32, _P, _P]),
+    "lisa_attn_st_open": (_i32, [ctypes.c_char_p, ctypes.POINTER(_P)]),
+    "lisa_attn_st_close": (_i32, [_P]),
+    "lisa_attn_st_count": (_i32, [_P]),
+    "lisa_attn_st_find": (_i32, [_P, ctypes.c_char_p]),
+    "lisa_attn_st_info": (_i32, [_P, _i32, ctypes.c_char_p, _sz, ctypes.POINTER(_i32), ctypes.POINTER(ctypes.c_uint64),
+                                 _i32, ctypes.POINTER(_i32), ctypes.POINTER(ctypes.c_uint64),
+                                 ctypes.POINTER(ctypes.c_uint64)]),
+    "lisa_attn_st_host_ptr": (_i32, [_P, _i32, ctypes.POINTER(_P)]),
+    "lisa_attn_st_upload": (_i32, [_P, _i32, _P, _sz, _P]),
     "lisa_attn_dev_count": (_i32, [ctypes.POINTER(_i32)]),
     "lisa_attn_dev_info": (_i32, [_i32, ctypes.c_char_p, _sz, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(_i32)]),
     "lisa_attn_dev_select": (_i32, [_i32]),
@@ -457,3 +466,119 @@ def qmv_u4(x, projections, out=None, stream=None):
     _check("lisa_attn_qmv_u4",
            load_library().lisa_attn_qmv_u4(len(projections), arr, rows, k, _ptr(x.contiguous()), _stream_ptr(stream)))
     return outs
+
+
+# ---- safetensors shards and the weight index ----------------------------------
+
+ST_DTYPES = ["BOOL", "U8", "U16", "I16", "F16", "BF16", "U32", "I32", "F32", "U64", "F64"]
+
+
+class Shard:
+    """One memory-mapped safetensors file (lisa_attn_st_*; the reference's
+    format::safetensor::Shard, src/format/safetensor.rs:17-41)."""
+
+    def __init__(self, path: str):
+        self.lib = load_library()
+        h = _P()
+        _check("lisa_attn_st_open", self.lib.lisa_attn_st_open(os.fsencode(path), ctypes.byref(h)))
+        self._h = h
+        self.path = path
+        self.tensors = {}
+        for i in range(self.lib.lisa_attn_st_count(h)):
+            name = ctypes.create_string_buffer(512)
+            dt, nd = _i32(), _i32()
+            shape = (ctypes.c_uint64 * 8)()
+            off, nb = ctypes.c_uint64(), ctypes.c_uint64()
+            _check("lisa_attn_st_info", self.lib.lisa_attn_st_info(h, i, name, 512, ctypes.byref(dt), shape, 8,
+                                                                   ctypes.byref(nd), ctypes.byref(off),
+                                                                   ctypes.byref(nb)))
+            self.tensors[name.value.decode()] = {"index": i, "dtype": ST_DTYPES[dt.value],
+                                                 "shape": [shape[j] for j in range(nd.value)],
+                                                 "offset": off.value, "len": nb.value}
+
+    def host_bytes(self, name: str) -> bytes:
+        t = self.tensors[name]
+        p = _P()
+        _check("lisa_attn_st_host_ptr", self.lib.lisa_attn_st_host_ptr(self._h, t["index"], ctypes.byref(p)))
+        return ctypes.string_at(p.value, t["len"])
+
+    def upload(self, name: str, dst, stream=None) -> None:
+        t = self.tensors[name]
+        _check("lisa_attn_st_upload", self.lib.lisa_attn_st_upload(
+            self._h, t["index"], _ptr(dst), dst.numel() * dst.element_size(), _stream_ptr(stream)))
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            self.lib.lisa_attn_st_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class WeightIndex:
+    """Tensor name -> (shard, slot) over several shards, as
+    model::weights::WeightIndex (src/model/weights.rs:16-81): a name present in
+    two shards is an error; rows(name, first, count) slices along dim 0."""
+
+    def __init__(self, paths):
+        self.shards = [Shard(p) for p in paths]
+        self.slots = {}
+        for si, sh in enumerate(self.shards):
+            for name, t in sh.tensors.items():
+                if name in self.slots:
+                    raise ValueError(f"duplicate tensor {name}")
+                self.slots[name] = (si, t)
+
+    def __len__(self):
+        return len(self.slots)
+
+    def slot(self, name):
+        s = self.slots.get(name)
+        return None if s is None else s[1]
+
+    def bytes(self, name):
+        s = self.slots.get(name)
+        return None if s is None else self.shards[s[0]].host_bytes(name)
+
+    def rows(self, name, first, count):
+        t = self.slot(name)
+        if t is None or not t["shape"]:
+            return None
+        n = t["shape"][0]
+        if first + count > n or t["len"] % n:
+            return None
+        rb = t["len"] // n
+        return self.bytes(name)[first * rb:(first + count) * rb]
+
+    def device_tensor(self, name, device=None, stream=None):
+        """Upload one tensor into a new torch device tensor of its dtype
+        (U32 as int32, BF16 as bfloat16)."""
+        import torch
+
+        t = self.slot(name)
+        if t is None:
+            raise KeyError(name)
+        dt = {"BF16": torch.bfloat16, "F16": torch.float16, "F32": torch.float32, "U32": torch.int32,
+              "I32": torch.int32, "U8": torch.uint8, "BOOL": torch.bool, "I16": torch.int16, "U16": torch.int16,
+              "F64": torch.float64, "U64": torch.int64}[t["dtype"]]
+        out = torch.empty(t["shape"], dtype=dt, device=device if device is not None else "cuda")
+        self.shards[self.slots[name][0]].upload(name, out, stream)
+        return out
+
+    def q4_projection(self, prefix, device=None):
+        """An affine-u4 linear layer stored as <prefix>.weight (U32 [n, k/8]),
+        <prefix>.scales and <prefix>.biases (BF16 [n, k/64]), as MLX writes
+        them; returns device tensors (packed, scales, biases) for qmv_u4."""
+        w, s, b = (self.slot(prefix + suf) for suf in (".weight", ".scales", ".biases"))
+        if w is None or s is None or b is None:
+            raise KeyError(prefix)
+        if w["dtype"] != "U32" or s["dtype"] != "BF16" or b["dtype"] != "BF16" or len(w["shape"]) != 2:
+            raise ValueError(f"{prefix}: not an affine-u4 projection")
+        n, k8 = w["shape"]
+        if s["shape"] != [n, k8 // 8] or b["shape"] != [n, k8 // 8]:
+            raise ValueError(f"{prefix}: scales/biases shape does not match group size 64")
+        return tuple(self.device_tensor(prefix + suf, device) for suf in (".weight", ".scales", ".biases"))

@@ -109,3 +109,28 @@ def test_qmv_argument_errors():
     bad = (P * 1)(P(pk.data_ptr() + 4, sb.data_ptr(), sb.data_ptr(), out.data_ptr(), 8))
     assert lib.lisa_attn_qmv_u4(1, bad, 1, 128, x.data_ptr(), None) == lisa_attn.EINVAL    # misaligned
     torch.cuda.synchronize()
+
+
+def test_q4_projection_loaded_from_a_safetensors_shard(tmp_path):
+    """An MLX affine-u4 projection written as <name>.weight/.scales/.biases
+    into a shard, loaded through the weight index onto the device and run by
+    the QMV, against the oracle on the file's bytes."""
+    import struct, json
+    rng = np.random.default_rng(91)
+    n, k = 300, 1024
+    packed, scales, biases = random_proj(rng, n, k)
+    tens = {"model.layers.3.self_attn.q_proj.weight": ("U32", packed), "model.layers.3.self_attn.q_proj.scales":
+            ("BF16", scales), "model.layers.3.self_attn.q_proj.biases": ("BF16", biases)}
+    header, blob = {}, b""
+    for name, (dt, a) in tens.items():
+        header[name] = {"dtype": dt, "shape": list(a.shape), "data_offsets": [len(blob), len(blob) + a.nbytes]}
+        blob += a.tobytes()
+    h = json.dumps(header).encode()
+    path = tmp_path / "q.safetensors"
+    path.write_bytes(struct.pack("<Q", len(h)) + h + blob)
+    idx = lisa_attn.WeightIndex([str(path)])
+    proj = idx.q4_projection("model.layers.3.self_attn.q_proj")
+    x = O.f32_to_bf16(rng.standard_normal((1, k)).astype(np.float32))
+    (got,) = lisa_attn.qmv_u4(dev_bf16(x), [proj])
+    want = O.q4_qmv(x, packed, scales, biases)
+    assert np.abs(got.cpu().numpy() - want).max() <= 2e-5 * np.abs(want).max() + 1e-4
