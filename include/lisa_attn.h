@@ -321,6 +321,24 @@ typedef struct {
 } lisa_attn_q4_proj;
 int lisa_attn_qmv_u4(int n_proj, const lisa_attn_q4_proj* projs, int rows, int k, const uint16_t* x, void* stream);
 
+/* ---- Gated DeltaNet recurrence ---------------------------------------------
+ * The state recurrence of the linear-attention layers (gdn_recurrence,
+ * src/kernels/shaders/gdn.metal:245-330), head dim 128 for keys and values,
+ * value heads sharing key heads in groups of `repeat` (48 value heads over 16
+ * key heads in the model). For each of `steps` tokens t, value head h,
+ * value column c, with s = ssm_state[h][c][0..127]:
+ *   s *= decay[t][h]; delta = (v - s.k) * beta[t][h]; s += delta * k;
+ *   y[t][h*128 + c] = bf16(s.q)  (stored as f32)
+ * with k, q = k_norm, q_norm [t][kh*128 ..] (kh = h / repeat) and v =
+ * conv_out[t][2*key_dim + h*128 + c] (conv_out rows are 2*key_dim + value_dim
+ * floats). ssm_state f32 [value_heads][128][128] is updated in place. With
+ * slot_stride > 0 the state after token t is also written to
+ * state_slots + t * slot_stride (floats; >= value_heads*128*128). A call over
+ * n tokens equals n one-token calls bit for bit. */
+int lisa_attn_gdn_recurrence(int steps, int value_heads, int repeat, const float* conv_out, const float* q_norm,
+                             const float* k_norm, const float* beta, const float* decay, float* ssm_state, float* y,
+                             float* state_slots, size_t slot_stride, void* stream);
+
 /* ---- safetensors shards (weights) ------------------------------------------
  * Host-side reader of the checkpoint container (src/format/safetensor.rs:
  * 1-91): [u64 LE header length][JSON header][tensor bytes], data_offsets

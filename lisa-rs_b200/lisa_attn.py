@@ -72,6 +72,7 @@ SIGNATURES = {
     "lisa_attn_noalloc_check_device_error": (_i32, []),
     "lisa_attn_debug_wait_fault": (_i32, [_u32, _i32]),
     "lisa_attn_qmv_u4": (_i32, [_i32, _P, _i32, _i32, _P, _P]),
+    "lisa_attn_gdn_recurrence": (_i32, [_i32, _i32, _i32, _P, _P, _P, _P, _P, _P, _P, _P, _sz, _P]),
     "lisa_attn_st_open": (_i32, [ctypes.c_char_p, ctypes.POINTER(_P)]),
     "lisa_attn_st_close": (_i32, [_P]),
     "lisa_attn_st_count": (_i32, [_P]),
@@ -582,3 +583,15 @@ class WeightIndex:
         if s["shape"] != [n, k8 // 8] or b["shape"] != [n, k8 // 8]:
             raise ValueError(f"{prefix}: scales/biases shape does not match group size 64")
         return tuple(self.device_tensor(prefix + suf, device) for suf in (".weight", ".scales", ".biases"))
+
+
+def gdn_recurrence(conv_out, q_norm, k_norm, beta, decay, state, y, value_heads=48, repeat=3, slots=None,
+                   stream=None):
+    """lisa_attn_gdn_recurrence over conv_out.shape[0] tokens (f32 tensors);
+    updates `state` in place and writes `y`; `slots` [steps, value_heads*128*128]
+    receives the state after every token when given."""
+    steps = conv_out.shape[0]
+    stride = slots[0].numel() if slots is not None else 0
+    _check("lisa_attn_gdn_recurrence", load_library().lisa_attn_gdn_recurrence(
+        steps, value_heads, repeat, _ptr(conv_out), _ptr(q_norm), _ptr(k_norm), _ptr(beta), _ptr(decay),
+        _ptr(state), _ptr(y), _ptr(slots), stride, _stream_ptr(stream)))

@@ -166,3 +166,27 @@ def q4_qmv(x_bits, packed, scale_bits, bias_bits):
     xs = x.reshape(m_rows, k // 64, 64).sum(-1)
     out = (xq * s[None]).sum(-1) + (xs[:, None, :] * b[None]).sum(-1)
     return out.astype(np.float32)
+
+
+# ---- Gated DeltaNet recurrence (numpy) ----------------------------------------
+
+def gdn_recurrence(conv_out, q, k, beta, decay, state, value_heads=48, repeat=3):
+    """gdn_recurrence (src/kernels/shaders/gdn.metal:245-330) in float64:
+    per token s *= decay; delta = (v - s.k) * beta; s += delta k; y = bf16(s.q).
+    state [value_heads, 128, 128] (value col, key dim); returns (y [T, vd]
+    float32 bf16-rounded, new state float64)."""
+    D = 128
+    kd = value_heads // repeat * D
+    s = np.asarray(state, np.float64).copy()
+    T = conv_out.shape[0]
+    y = np.zeros((T, value_heads * D), np.float32)
+    for t in range(T):
+        kt = k[t].astype(np.float64).reshape(-1, D)[np.arange(value_heads) // repeat]  # [vh, 128]
+        qt = q[t].astype(np.float64).reshape(-1, D)[np.arange(value_heads) // repeat]
+        v = conv_out[t, 2 * kd:].astype(np.float64).reshape(value_heads, D)
+        s *= decay[t].astype(np.float64)[:, None, None]
+        kv = np.einsum("hcd,hd->hc", s, kt)
+        delta = (v - kv) * beta[t].astype(np.float64)[:, None]
+        s += delta[:, :, None] * kt[:, None, :]
+        y[t] = bf16_to_f32(f32_to_bf16(np.einsum("hcd,hd->hc", s, qt).reshape(-1).astype(np.float32)))
+    return y, s
