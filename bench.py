@@ -540,6 +540,42 @@ def bench_qmv(args, world):
     return us, nbytes
 
 
+def bench_gdn(args, world):
+    """The Gated DeltaNet recurrence of one decode token (lisa_attn_gdn_recurrence,
+    M=1, 48 value heads x 128 x 128 f32 state) for the 48 linear-attention
+    layers of a step, each with its own state (48 x 3 MB, larger than L2);
+    one CUDA graph per step. Returns (µs per layer call, algorithmic bytes)."""
+    import torch
+
+    import lisa_attn
+
+    vh, kh, d, layers = 48, 16, 128, 48
+    conv_dim = 2 * kh * d + vh * d
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(0x5EED + 12)
+    states = [0.1 * torch.randn((vh, d, d), generator=gen, device="cuda") for _ in range(layers)]
+    conv = torch.randn((1, conv_dim), generator=gen, device="cuda")
+    q = torch.randn((1, kh * d), generator=gen, device="cuda") / d
+    k = torch.randn((1, kh * d), generator=gen, device="cuda") / d ** 0.5
+    beta = torch.sigmoid(torch.randn((1, vh), generator=gen, device="cuda"))
+    decay = torch.full((1, vh), 0.95, device="cuda")
+    y = torch.empty((1, vh * d), device="cuda")
+    stream = torch.cuda.current_stream()
+    lisa_attn.gdn_recurrence(conv, q, k, beta, decay, states[0], y, vh, vh // kh, stream=stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    cs = torch.cuda.Stream()
+    with torch.cuda.stream(cs):
+        with torch.cuda.graph(graph, stream=cs):
+            for st in states:
+                lisa_attn.gdn_recurrence(conv, q, k, beta, decay, st, y, vh, vh // kh, stream=cs)
+    torch.cuda.synchronize()
+    ms = timed(graph.replay, args.steps, args.warmup, world, stream)
+    us = ms * 1000.0 / args.steps / layers
+    nbytes = 2 * vh * d * d * 4 + (conv_dim + 2 * kh * d + 2 * vh + vh * d) * 4
+    return us, nbytes
+
+
 def emit(line: dict) -> None:
     print(json.dumps(line), flush=True)
 
@@ -643,6 +679,7 @@ def main():
     pf_ms, pf_ms_eager = bench_prefill(args, world)
     torch.cuda.empty_cache()
     qmv_us, qmv_bytes = bench_qmv(args, world)
+    gdn_us, gdn_bytes = bench_gdn(args, world)
     torch.cuda.empty_cache()
     blocks = {}
     if not args.decode_only:
@@ -710,6 +747,12 @@ def main():
                    "us_per_launch": round(qmv_us, 3), "algorithmic_bytes": qmv_bytes,
                    "roofline": {"bound": "hbm", "achieved": round(qmv_gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                                 "frac": round(qmv_gbs / pk["hbm_gbs"], 4), "traffic": None}}
+    gdn_gbs = gdn_bytes / (gdn_us * 1e-6) / 1e9
+    line["gdn"] = {"workload": "Gated DeltaNet recurrence of one decode token for 48 layers, each its own 3 MB f32 "
+                               "state (144 MB > L2), 48 launches per CUDA graph (lisa_attn_gdn_recurrence)",
+                   "us_per_layer": round(gdn_us, 3), "algorithmic_bytes": gdn_bytes,
+                   "roofline": {"bound": "hbm", "achieved": round(gdn_gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                                "frac": round(gdn_gbs / pk["hbm_gbs"], 4), "traffic": None}}
     line.update(blocks)
     emit(line)
     if world > 1:
