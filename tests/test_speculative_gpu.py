@@ -139,3 +139,99 @@ def test_block3_loop_equals_sequential_greedy(seed):
     assert spec.runner.position() == seq.runner.position() == n
     for a, b in zip(spec.runner.kv_cache(0), seq.runner.kv_cache(0)):
         assert torch.equal(a[:, :n], b[:, :n])
+
+
+def mtp_reconcile_plan(draft_count, round_appended, accepted):
+    """speculative/mod.rs:49-65: keep the drafts already appended this round
+    that were accepted, replay the accepted ones not in the cache, then the
+    replacement / bonus token."""
+    assert accepted <= draft_count and round_appended <= draft_count
+    keep = min(accepted, round_appended)
+    replay = [("draft", i) for i in range(keep, accepted)] + [("replacement", None)]
+    return round_appended - keep, replay
+
+
+class ToyDrafter(ToyTarget):
+    """The MTP drafter's attention: a 1-layer context of its own (own toy
+    embedding), advanced one position per forward and trimmed by the
+    reconcile plan; `tokens` is the token sequence its live KV prefix must
+    hold."""
+
+    def __init__(self, seed, capacity):
+        super().__init__(seed + 777, capacity)
+        self.tokens = []
+
+    def forward(self, token):
+        out = self.runner.forward_decode(0, *self.inputs([token]), self.w)
+        self.runner.advance(1)
+        self.tokens.append(token)
+        return self.next_tokens(out)[0]
+
+    def trim_state(self, n):
+        self.runner.trim_state(n)
+        del self.tokens[len(self.tokens) - n:]
+
+
+@pytest.mark.parametrize("seed", [4, 5])
+def test_block3_loop_with_a_drafter_context(seed):
+    """run_block3_loop (speculative/mod.rs:102-198) with the drafter side too:
+    the drafter appends its forwards to its own 1-layer context, and after
+    every verify applies mtp_reconcile_plan + trim_state (mod.rs:167) and
+    replays the plan's last entry. The emitted tokens equal sequential greedy
+    decoding, and the drafter's live KV prefix equals a fresh drafter that
+    decoded the same token sequence one position at a time."""
+    cap = PROMPT + 2 * MAX_TOKENS + 16
+    rng = np.random.default_rng(9100 + seed)
+    prompt = rng.integers(0, VOCAB, size=PROMPT).tolist()
+    seq = ToyTarget(seed, cap)
+    bonus = seq.prefill(prompt)
+    want = greedy_sequential(seq, bonus, MAX_TOKENS)
+
+    spec = ToyTarget(seed, cap)
+    assert spec.prefill(prompt) == bonus
+    mtp = ToyDrafter(seed, cap)
+    mix = np.random.default_rng(600 + seed)
+
+    def draft(own, n_emitted):
+        truth = want[n_emitted] if n_emitted < len(want) else 0
+        return truth if mix.random() < 0.6 else own
+
+    tokens, seed_tok, rounds, trims = [], None, 0, 0
+    while len(tokens) < MAX_TOKENS:
+        remaining = MAX_TOKENS - len(tokens)
+        if remaining < 3:
+            for _ in range(remaining):
+                bonus = spec.forward_token_decode(bonus)
+                tokens.append(bonus)
+            break
+        if seed_tok is not None:
+            d0 = seed_tok
+            d1 = draft(mtp.forward(d0), len(tokens) + 1)
+            round_appended = 1
+        else:
+            d0 = draft(mtp.forward(bonus), len(tokens))
+            d1 = draft(mtp.forward(d0), len(tokens) + 1)
+            round_appended = 2
+        drafts = [d0, d1]
+        target = spec.verify_block3([bonus, d0, d1])
+        accepted, emitted = accept_greedy(drafts, target)
+        spec.runner.commit_verified_prefix(accepted + 1)
+        trim, replay = mtp_reconcile_plan(2, round_appended, accepted)
+        mtp.trim_state(trim)
+        trims += trim
+        kind, index = replay[-1]
+        token = drafts[index] if kind == "draft" else emitted[-1]
+        seed_tok = draft(mtp.forward(token), len(tokens) + len(emitted))
+        bonus = emitted[-1]
+        tokens.extend(emitted)
+        rounds += 1
+    assert tokens == want
+    assert rounds > 0 and trims > 0
+    # the drafter's live prefix: same rows as a fresh drafter fed mtp.tokens one by one
+    fresh = ToyDrafter(seed, cap)
+    for t in mtp.tokens:
+        fresh.forward(t)
+    n = len(mtp.tokens)
+    assert mtp.runner.position() == fresh.runner.position() == n
+    for a, b in zip(mtp.runner.kv_cache(0), fresh.runner.kv_cache(0)):
+        assert torch.equal(a[:, :n], b[:, :n])
