@@ -307,8 +307,9 @@ int lisa_attn_debug_wait_fault(uint32_t wait_limit_us, int withhold_loads);
  * One launch serves up to LISA_ATTN_QMV_MAX_PROJ projections of the same x
  * (q_proj + k_proj + v_proj as fused3 does; their outputs are what
  * lisa_attn_decode takes as q_gate, k, v with LISA_DTYPE_F32). k must be a
- * multiple of 64 in 64..LISA_ATTN_QMV_MAX_K, packed 16-byte aligned;
- * LISA_EINVAL otherwise. */
+ * multiple of 64 in 64..LISA_ATTN_QMV_MAX_K, x and packed 16-byte aligned,
+ * and x must fit in shared memory beside two weight stages (rows x k up to
+ * 4 x 6144 or 2 x 8192); LISA_EINVAL otherwise. */
 #define LISA_ATTN_QMV_MAX_PROJ 4
 #define LISA_ATTN_QMV_MAX_ROWS 4
 #define LISA_ATTN_QMV_MAX_K 8192

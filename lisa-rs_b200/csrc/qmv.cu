@@ -12,16 +12,18 @@
 //
 // B200 layout. The kernel is bound by streaming the packed weights from HBM
 // (K/2 + K/16 bytes per row). One launch covers up to four projections of the
-// same x (q, k, v fused). A CTA of 8 warps owns 32 consecutive rows of one
-// projection (16 for x with several rows); warp w takes 4 rows (2), and lane l takes the 32-element chunks
+// same x (q, k, v fused). A persistent grid (two or three CTAs of 8 warps per SM)
+// walks the rows; lane l of a warp takes the 32-element chunks
 // c = l, l + 32, ... of K: one 16-byte load of packed weights per (row, chunk)
 // (32 nibbles), its group's scale and bias, so the warp reads each row with
-// fully coalesced 512-byte requests, four rows in flight at once. x is staged
+// fully coalesced 512-byte requests, the next row's already in flight. x is staged
 // in shared memory as f32, one 32-element chunk per 36-float slot, so a
 // quarter warp's 16-byte reads of 8 consecutive chunks hit 8 disjoint bank
 // quads; the per-chunk sums of x (for the bias term) sit after it.
 #include <cuda_runtime.h>
 #include <stdint.h>
+
+#include <algorithm>
 
 #include "../../include/lisa_attn.h"
 #include "common.cuh"
@@ -31,7 +33,8 @@ namespace lisa {
 
 namespace {
 
-constexpr int QMV_WARPS = 8;  // rows per warp: 4 for one x row, 2 for 2..4 rows (register budget)
+constexpr int QMV_BR = 16;     // rows per stage = consumer warps
+constexpr int QMV_STAGES = 4;  // weight blocks in flight per SM (fewer when x is large)
 constexpr int QMV_MAX_M = LISA_ATTN_QMV_MAX_ROWS;
 constexpr int QMV_MAX_PROJ = LISA_ATTN_QMV_MAX_PROJ;
 constexpr int QMV_SLOT = 36;  // floats per staged 32-element chunk of x
@@ -42,103 +45,178 @@ struct QmvProj {
   const uint16_t* biases;   // [N][K/64] bf16
   float* out;               // [M][N]
   int n;
-  int cta0;                 // first CTA of this projection
+  int grp0;                 // first row block of this projection in the launch's list
 };
 
 struct QmvParams {
-  int m, k, n_proj;
-  const uint16_t* x;        // [M][K] bf16
+  int m, k, n_proj, groups;  // groups: blocks of QMV_BR rows over all projections
+  int stages;                // ring depth (2..QMV_STAGES, as shared memory allows)
+  const uint16_t* x;         // [M][K] bf16
   QmvProj proj[QMV_MAX_PROJ];
 };
 
 }  // namespace
 
-template <int M, int RPW = (M == 1 ? 4 : 2)>
-__global__ void __launch_bounds__(32 * QMV_WARPS, 2) qmv_u4_kernel(const __grid_constant__ QmvParams p) {
-  extern __shared__ float qmv_smem[];
+// Persistent, one CTA per SM: a producer warp streams blocks of QMV_BR
+// consecutive weight rows of the projections (packed words, scales and biases
+// by bulk copies) through a ring of up to QMV_STAGES shared-memory stages
+// (mbarrier full / empty), and QMV_BR consumer warps dequantise and dot them
+// against x (staged once per CTA as f32). The ring keeps the stages' weights
+// in flight per SM whatever the registers.
+template <int M>
+__global__ void __launch_bounds__(32 * (QMV_BR + 1), 1) qmv_u4_kernel(const __grid_constant__ QmvParams p) {
+  extern __shared__ __align__(16) uint8_t qmv_smem_raw[];
   const int K = p.k;
-  const int chunks = K / 32;
-  // xs[m][c][i] = x[m][32 c + i] (slot stride QMV_SLOT floats); xsum[m][c]
-  float* xs = qmv_smem;
-  float* xsum = qmv_smem + (size_t)M * chunks * QMV_SLOT;
-  pdl_wait_primary();
-  pdl_launch_dependents();
-  for (int e = threadIdx.x; e < M * K; e += blockDim.x) {
-    const int m = e / K, k = e % K;
-    xs[((size_t)m * chunks + (k >> 5)) * QMV_SLOT + (k & 31)] = bf16_bits_to_f32(p.x[e]);
-  }
-  __syncthreads();
-  for (int e = threadIdx.x; e < M * chunks; e += blockDim.x) {
-    const float* sl = xs + (size_t)e * QMV_SLOT;
-    float s = 0.f;
-    for (int i = 0; i < 32; ++i) s += sl[i];
-    xsum[e] = s;
-  }
-  __syncthreads();
-
-  int pi = 0;
-  while (pi + 1 < p.n_proj && (int)blockIdx.x >= p.proj[pi + 1].cta0) ++pi;
-  const QmvProj& pr = p.proj[pi];
+  const int chunks = K / 32, groups_k = K / 64;
+  const size_t row_bytes = (size_t)K / 2;
+  // [x: M][chunks][QMV_SLOT] f32 | xsum [M][chunks] | stages | barriers
+  float* xs = reinterpret_cast<float*>(qmv_smem_raw);
+  float* xsum = xs + (size_t)M * chunks * QMV_SLOT;
+  const size_t x_bytes = (((size_t)M * chunks * (QMV_SLOT + 1)) * sizeof(float) + 127) & ~size_t(127);
+  const size_t sg_bytes = ((size_t)QMV_BR * groups_k * 2 + 15) & ~size_t(15);  // bf16 scales (then biases) of a block
+  const size_t stage_bytes = (QMV_BR * row_bytes + 2 * sg_bytes + 127) & ~size_t(127);
+  uint8_t* stages = qmv_smem_raw + x_bytes;
+  const int n_st = p.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(stages + n_st * stage_bytes);
+  uint64_t* empty = full + n_st;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row0 = ((int)blockIdx.x - pr.cta0) * (RPW * QMV_WARPS) + warp * RPW;
-  if (row0 >= pr.n) return;
-  const int groups = K / 64;
-  const int words = K / 8;
+  const int n_blocks = p.groups;  // blocks of QMV_BR rows over all projections
 
-  float acc[RPW][M];
-#pragma unroll
-  for (int r = 0; r < RPW; ++r)
-#pragma unroll
-    for (int m = 0; m < M; ++m) acc[r][m] = 0.f;
-
-  for (int c = lane; c < chunks; c += 32) {
-    uint4 w[RPW];
-    float sc[RPW], bi[RPW];
-#pragma unroll
-    for (int r = 0; r < RPW; ++r) {
-      const int row = min(row0 + r, pr.n - 1);  // rows past N repeat the last one, never stored
-      w[r] = __ldcs(reinterpret_cast<const uint4*>(pr.packed + (size_t)row * words) + c);
-      sc[r] = bf16_bits_to_f32(__ldg(pr.scales + (size_t)row * groups + (c >> 1)));
-      bi[r] = bf16_bits_to_f32(__ldg(pr.biases + (size_t)row * groups + (c >> 1)));
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < n_st; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], QMV_BR);
     }
-#pragma unroll
-    for (int m = 0; m < M; ++m) {
-      const float4* xm = reinterpret_cast<const float4*>(xs + ((size_t)m * chunks + c) * QMV_SLOT);
-      float dot[RPW] = {};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float4 a = xm[2 * j], b4 = xm[2 * j + 1];
-        const float xv[8] = {a.x, a.y, a.z, a.w, b4.x, b4.y, b4.z, b4.w};
-#pragma unroll
-        for (int r = 0; r < RPW; ++r) {
-          const uint32_t word = (&w[r].x)[j];
-#pragma unroll
-          for (int b = 0; b < 8; ++b) dot[r] = fmaf(xv[b], (float)((word >> (4 * b)) & 0xfu), dot[r]);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == QMV_BR) {
+    // ---------------- producer ----------------
+    // The weights are never written by a kernel: streaming starts before the
+    // wait on the previous kernel (which may produce x).
+    int it = 0;
+    for (int blk = blockIdx.x; blk < n_blocks; blk += gridDim.x, ++it) {
+      const int s = it % n_st;
+      if (it >= n_st && !mbar_wait(&empty[s], ((it / n_st) - 1) & 1, nullptr, 0)) break;
+      int pi = 0;
+      while (pi + 1 < p.n_proj && blk >= p.proj[pi + 1].grp0) ++pi;
+      const QmvProj& pr = p.proj[pi];
+      const int row0 = (blk - pr.grp0) * QMV_BR;
+      const int nrows = min(QMV_BR, pr.n - row0);
+      uint8_t* st = stages + (size_t)s * stage_bytes;
+      // packed rows, scales and biases of the block are each contiguous:
+      // three bulk copies (sizes rounded down to 16 bytes; a short tail of the
+      // scales / biases is copied by the lanes)
+      const uint32_t pk_bytes = (uint32_t)(nrows * row_bytes);
+      const uint32_t g_bytes = (uint32_t)(nrows * groups_k * 2);
+      const uint32_t g_bulk = g_bytes & ~15u;
+      const uint8_t* sc_src = reinterpret_cast<const uint8_t*>(pr.scales + (size_t)row0 * groups_k);
+      const uint8_t* bi_src = reinterpret_cast<const uint8_t*>(pr.biases + (size_t)row0 * groups_k);
+      uint8_t* sc_dst = st + QMV_BR * row_bytes;
+      uint8_t* bi_dst = sc_dst + sg_bytes;
+      for (uint32_t b = g_bulk + 2 * lane; b < g_bytes; b += 64) {
+        *reinterpret_cast<uint16_t*>(sc_dst + b) = *reinterpret_cast<const uint16_t*>(sc_src + b);
+        *reinterpret_cast<uint16_t*>(bi_dst + b) = *reinterpret_cast<const uint16_t*>(bi_src + b);
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&full[s], pk_bytes + 2 * g_bulk);  // also publishes the lanes' tail stores
+        bulk_load(st, reinterpret_cast<const uint8_t*>(pr.packed) + (size_t)row0 * row_bytes, pk_bytes, &full[s]);
+        if (g_bulk) {
+          bulk_load(sc_dst, sc_src, g_bulk, &full[s]);
+          bulk_load(bi_dst, bi_src, g_bulk, &full[s]);
         }
       }
-      const float s = xsum[m * chunks + c];
-#pragma unroll
-      for (int r = 0; r < RPW; ++r) acc[r][m] += fmaf(sc[r], dot[r], bi[r] * s);
     }
+    return;
   }
+
+  pdl_wait_primary();
+  pdl_launch_dependents();
+  // x arrives as 16-byte vectors of 8 bf16 (a run of 8 never crosses a row)
+  for (int e8 = threadIdx.x; e8 < M * K / 8; e8 += 32 * QMV_BR) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(p.x) + e8);
+    const int m = (8 * e8) / K, k = 8 * e8 - m * K;
+    float4* dst = reinterpret_cast<float4*>(xs + ((size_t)m * chunks + (k >> 5)) * QMV_SLOT + (k & 31));
+    const float2 a = unpack_bf16x2(v.x), b = unpack_bf16x2(v.y), c2 = unpack_bf16x2(v.z), d = unpack_bf16x2(v.w);
+    dst[0] = make_float4(a.x, a.y, b.x, b.y);
+    dst[1] = make_float4(c2.x, c2.y, d.x, d.y);
+  }
+  named_bar_sync(1, 32 * QMV_BR);
+  for (int e = threadIdx.x; e < M * chunks; e += 32 * QMV_BR) {
+    const float* sl = xs + (size_t)e * QMV_SLOT;
+    float sum = 0.f;
+#pragma unroll 8
+    for (int i = 0; i < 32; ++i) sum += sl[i];
+    xsum[e] = sum;
+  }
+  named_bar_sync(1, 32 * QMV_BR);
+
+  // Consumer warp w takes row w of each stage; lane l the 32-element chunks
+  // l, l + 32, ... of K.
+  int it = 0;
+  for (int blk = blockIdx.x; blk < n_blocks; blk += gridDim.x, ++it) {
+    const int s = it % n_st;
+    if (!mbar_wait(&full[s], (it / n_st) & 1, nullptr, 0)) break;
+    int pi = 0;
+    while (pi + 1 < p.n_proj && blk >= p.proj[pi + 1].grp0) ++pi;
+    const QmvProj& pr = p.proj[pi];
+    const int row = (blk - pr.grp0) * QMV_BR + warp;
+    const uint8_t* st = stages + (size_t)s * stage_bytes;
+    if (row < pr.n) {
+      const uint4* wrow = reinterpret_cast<const uint4*>(st + (size_t)warp * row_bytes);
+      const uint16_t* scr = reinterpret_cast<const uint16_t*>(st + QMV_BR * row_bytes) + (size_t)warp * groups_k;
+      const uint16_t* bir =
+          reinterpret_cast<const uint16_t*>(st + QMV_BR * row_bytes + sg_bytes) + (size_t)warp * groups_k;
+      float acc[M];
 #pragma unroll
-  for (int r = 0; r < RPW; ++r)
+      for (int m = 0; m < M; ++m) acc[m] = 0.f;
+      for (int c = lane; c < chunks; c += 32) {
+        const uint4 w4 = wrow[c];
+        // nibble 2i is the low half of byte i, nibble 2i+1 the high half; a
+        // nibble placed in the low mantissa bits of 2^23 is 2^23 + q, and
+        // 2^23 + q - 2^23 = q exactly (no int -> float conversion)
+        float2 qv[16];
 #pragma unroll
-    for (int m = 0; m < M; ++m) {
-      float v = acc[r][m];
+        for (int wq = 0; wq < 4; ++wq) {
+          const uint32_t word = (&w4.x)[wq];
+          const uint32_t lo = word & 0x0F0F0F0Fu, hi = (word >> 4) & 0x0F0F0F0Fu;
 #pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-      acc[r][m] = v;
+          for (int i = 0; i < 4; ++i) {
+            const uint32_t sel = (uint32_t)i | 0x7540u;  // byte i of the nibbles, then 00 00 4B
+            qv[4 * wq + i] = fadd2(make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, sel)),
+                                               __uint_as_float(__byte_perm(hi, 0x4B000000u, sel))),
+                                   make_float2(-8388608.0f, -8388608.0f));
+          }
+        }
+        const float scale = bf16_bits_to_f32(scr[c >> 1]), bias = bf16_bits_to_f32(bir[c >> 1]);
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+          const float4* xm = reinterpret_cast<const float4*>(xs + ((size_t)m * chunks + c) * QMV_SLOT);
+          float2 dot = make_float2(0.f, 0.f);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 x4 = xm[q];
+            dot = ffma2(make_float2(x4.x, x4.y), qv[2 * q], dot);
+            dot = ffma2(make_float2(x4.z, x4.w), qv[2 * q + 1], dot);
+          }
+          acc[m] += fmaf(scale, dot.x + dot.y, bias * xsum[m * chunks + c]);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        float v = acc[m];
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+        if (lane == 0) pr.out[(size_t)m * pr.n + row] = v;
+      }
+    } else {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
     }
-  if (lane < RPW * M) {
-    const int r = lane / M, m = lane % M;
-    float v = 0.f;
-#pragma unroll
-    for (int rr = 0; rr < RPW; ++rr)
-#pragma unroll
-      for (int mm = 0; mm < M; ++mm)
-        if (rr == r && mm == m) v = acc[rr][mm];
-    if (row0 + r < pr.n) pr.out[(size_t)m * pr.n + row0 + r] = v;
   }
 }
 
@@ -146,46 +224,70 @@ __global__ void __launch_bounds__(32 * QMV_WARPS, 2) qmv_u4_kernel(const __grid_
 
 using namespace lisa;
 
+namespace {
+
+constexpr size_t kSmemMax = 227 * 1024;
+
+size_t qmv_x_bytes(int m, int k) { return ((size_t)m * (k / 32) * (QMV_SLOT + 1) * sizeof(float) + 127) & ~size_t(127); }
+size_t qmv_stage_bytes(int k) {
+  const size_t sg = ((size_t)QMV_BR * (k / 64) * 2 + 15) & ~size_t(15);
+  return ((size_t)QMV_BR * k / 2 + 2 * sg + 127) & ~size_t(127);
+}
+int qmv_stages(int m, int k) {
+  const size_t room = kSmemMax - qmv_x_bytes(m, k) - 2 * QMV_STAGES * sizeof(uint64_t);
+  return (int)std::max<size_t>(2, std::min<size_t>(QMV_STAGES, room / qmv_stage_bytes(k)));
+}
+size_t qmv_smem_bytes(int m, int k) {
+  const int st = qmv_stages(m, k);
+  return qmv_x_bytes(m, k) + st * qmv_stage_bytes(k) + 2 * st * sizeof(uint64_t)
+}
+
+template <int M>
+cudaError_t launch_m(cudaLaunchConfig_t& cfg, const QmvParams& p) {
+  static SmemAttr attr_once;  // per kernel and device, for the largest request
+  const cudaError_t e = attr_once.ensure(qmv_u4_kernel<M>, (int)kSmemMax);
+  return e == cudaSuccess ? cudaLaunchKernelEx(&cfg, qmv_u4_kernel<M>, p) : e;
+}
+
+}  // namespace
+
 #pragma GCC visibility push(default)
 extern "C" int lisa_attn_qmv_u4(int n_proj, const lisa_attn_q4_proj* projs, int rows, int k, const uint16_t* x,
                                 void* stream) {
-  if (n_proj < 1 || n_proj > QMV_MAX_PROJ || !projs || !x) return LISA_EINVAL;
+  if (n_proj < 1 || n_proj > QMV_MAX_PROJ || !projs || !x || ((uintptr_t)x & 15)) return LISA_EINVAL;
   if (rows < 1 || rows > QMV_MAX_M || k < 64 || k % 64 != 0 || k > LISA_ATTN_QMV_MAX_K) return LISA_EINVAL;
   QmvParams p = {};
   p.m = rows;
   p.k = k;
   p.n_proj = n_proj;
   p.x = x;
-  int ctas = 0;
+  int blocks = 0;  // blocks of QMV_BR rows over all projections
   for (int i = 0; i < n_proj; ++i) {
     const lisa_attn_q4_proj& q = projs[i];
     if (!q.packed || !q.scales || !q.biases || !q.out || q.n < 1) return LISA_EINVAL;
-    if ((uintptr_t)q.packed & 15) return LISA_EINVAL;  // 16-byte loads of packed words
-    p.proj[i] = QmvProj{static_cast<const uint32_t*>(q.packed), q.scales, q.biases, q.out, q.n, ctas};
-    const int rows_per_cta = (rows == 1 ? 4 : 2) * QMV_WARPS;
-    ctas += (q.n + rows_per_cta - 1) / rows_per_cta;
+    if ((uintptr_t)q.packed & 15) return LISA_EINVAL;  // bulk copies of packed rows
+    p.proj[i] = QmvProj{static_cast<const uint32_t*>(q.packed), q.scales, q.biases, q.out, q.n, blocks};
+    blocks += (q.n + QMV_BR - 1) / QMV_BR;
   }
-  const size_t smem = ((size_t)rows * (k / 32) * QMV_SLOT + (size_t)rows * (k / 32)) * sizeof(float);
-  // the attribute is set once per device, for the largest request
-  constexpr int kMaxSmem = (QMV_MAX_M * (LISA_ATTN_QMV_MAX_K / 32) * QMV_SLOT + QMV_MAX_M * (LISA_ATTN_QMV_MAX_K / 32)) *
-                           (int)sizeof(float);
+  p.groups = blocks;
+  p.stages = qmv_stages(rows, k);
+  if (qmv_smem_bytes(rows, k) > kSmemMax) return LISA_EINVAL;  // x and two weight stages must fit
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(ctas);
-  cfg.blockDim = dim3(32 * QMV_WARPS);
-  cfg.dynamicSmemBytes = smem;
+  cfg.gridDim = dim3(std::min(current_device_sms(), blocks));
+  cfg.blockDim = dim3(32 * (QMV_BR + 1));
+  cfg.dynamicSmemBytes = qmv_smem_bytes(rows, k);
   cfg.stream = static_cast<cudaStream_t>(stream);
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  static SmemAttr a1, a2, a3, a4;
   cudaError_t e;
   switch (rows) {
-    case 1: e = a1.ensure(qmv_u4_kernel<1>, kMaxSmem); if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, qmv_u4_kernel<1>, p); break;
-    case 2: e = a2.ensure(qmv_u4_kernel<2>, kMaxSmem); if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, qmv_u4_kernel<2>, p); break;
-    case 3: e = a3.ensure(qmv_u4_kernel<3>, kMaxSmem); if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, qmv_u4_kernel<3>, p); break;
-    default: e = a4.ensure(qmv_u4_kernel<4>, kMaxSmem); if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, qmv_u4_kernel<4>, p); break;
+    case 1: e = launch_m<1>(cfg, p); break;
+    case 2: e = launch_m<2>(cfg, p); break;
+    case 3: e = launch_m<3>(cfg, p); break;
+    default: e = launch_m<4>(cfg, p); break;
   }
   return e == cudaSuccess ? LISA_OK : LISA_ECUDA;
 }

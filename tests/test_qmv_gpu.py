@@ -61,11 +61,12 @@ def test_fused_qkv_projection_sizes(rows):
         assert err <= 2e-5 * np.abs(want).max() + 1e-4, err
 
 
-@pytest.mark.parametrize("n,k", [(19, 128), (33, 64), (100, 6144), (5120, 6144), (7, 8192)])
-def test_odd_shapes(n, k):
+@pytest.mark.parametrize("n,k,rows", [(19, 128, 3), (33, 64, 3), (100, 6144, 3), (5120, 6144, 3), (5120, 6144, 1),
+                                      (7, 8192, 2)])
+def test_odd_shapes(n, k, rows):
     """Tail rows, K not a multiple of 1024, the o_proj shape (5120 x 6144)."""
     rng = np.random.default_rng(n + k)
-    x = O.f32_to_bf16(rng.standard_normal((3, k)).astype(np.float32))
+    x = O.f32_to_bf16(rng.standard_normal((rows, k)).astype(np.float32))
     proj = random_proj(rng, n, k)
     (got,) = run(x, [proj])
     want = O.q4_qmv(x, *proj)
@@ -106,6 +107,9 @@ def test_qmv_argument_errors():
     assert lib.lisa_attn_qmv_u4(1, good, 5, 128, x.data_ptr(), None) == lisa_attn.EINVAL   # rows > 4
     assert lib.lisa_attn_qmv_u4(1, good, 1, 96, x.data_ptr(), None) == lisa_attn.EINVAL    # k % 64
     assert lib.lisa_attn_qmv_u4(0, good, 1, 128, x.data_ptr(), None) == lisa_attn.EINVAL
+    assert lib.lisa_attn_qmv_u4(1, good, 1, 128, x.data_ptr() + 2, None) == lisa_attn.EINVAL  # misaligned x
+    x8 = torch.zeros((3, 8192), dtype=torch.bfloat16, device="cuda")
+    assert lib.lisa_attn_qmv_u4(1, good, 3, 8192, x8.data_ptr(), None) == lisa_attn.EINVAL  # x too large
     bad = (P * 1)(P(pk.data_ptr() + 4, sb.data_ptr(), sb.data_ptr(), out.data_ptr(), 8))
     assert lib.lisa_attn_qmv_u4(1, bad, 1, 128, x.data_ptr(), None) == lisa_attn.EINVAL    # misaligned
     torch.cuda.synchronize()
