@@ -239,7 +239,7 @@ int qmv_stages(int m, int k) {
 }
 size_t qmv_smem_bytes(int m, int k) {
   const int st = qmv_stages(m, k);
-  return qmv_x_bytes(m, k) + st * qmv_stage_bytes(k) + 2 * st * sizeof(uint64_t)
+  return qmv_x_bytes(m, k) + st * qmv_stage_bytes(k) + 2 * st * sizeof(uint64_t);
 }
 
 template <int M>
