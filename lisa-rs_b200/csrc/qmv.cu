@@ -12,14 +12,15 @@
 //
 // B200 layout. The kernel is bound by streaming the packed weights from HBM
 // (K/2 + K/16 bytes per row). One launch covers up to four projections of the
-// same x (q, k, v fused). A persistent grid (two or three CTAs of 8 warps per SM)
-// walks the rows; lane l of a warp takes the 32-element chunks
-// c = l, l + 32, ... of K: one 16-byte load of packed weights per (row, chunk)
-// (32 nibbles), its group's scale and bias, so the warp reads each row with
-// fully coalesced 512-byte requests, the next row's already in flight. x is staged
-// in shared memory as f32, one 32-element chunk per 36-float slot, so a
-// quarter warp's 16-byte reads of 8 consecutive chunks hit 8 disjoint bank
-// quads; the per-chunk sums of x (for the bias term) sit after it.
+// same x (q, k, v fused). One persistent CTA per SM: a producer warp moves
+// blocks of 16 consecutive rows (packed words, scales, biases: three bulk
+// copies) through a ring of shared-memory stages, and 16 consumer warps take
+// one row each: lane l dequantises the 32-element chunks l, l + 32, ... (a
+// nibble dropped into the mantissa of 2^23, minus 2^23: no int -> float
+// conversion) and dots them with x in packed f32x2 FMAs. x is staged in shared
+// memory as f32, one 32-element chunk per 36-float slot, so a quarter warp's
+// 16-byte reads of 8 consecutive chunks hit 8 disjoint bank quads; the
+// per-chunk sums of x (for the bias term) sit after it.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
