@@ -543,6 +543,8 @@ __global__ void __launch_bounds__(CMB_THREADS) decode_combine_kernel(const Decod
         }
       }
     }
+    // every lane's peer stores are ordered (system scope) before the flag
+    __threadfence_system();
     __syncwarp();
     if (slot == 0) {
       __threadfence_system();
