@@ -543,11 +543,11 @@ __global__ void __launch_bounds__(CMB_THREADS) decode_combine_kernel(const Decod
         }
       }
     }
-    // every lane's peer stores are ordered (system scope) before the flag
-    __threadfence_system();
+    // The warp barrier orders every lane's peer stores before lane 0's
+    // release store of the flag (release is cumulative at system scope), so
+    // no separate fence is needed.
     __syncwarp();
     if (slot == 0) {
-      __threadfence_system();
       const size_t f = (((size_t)x.rank * 3 + m) * KVH + kvh) * 32 + db;
       for (int dst = 0; dst < x.world; ++dst) st_release_sys(x.flags[dst] + f, epoch);
     }
@@ -608,6 +608,8 @@ __global__ void __launch_bounds__(256) merge_exchange_kernel(const XchgDev* xp, 
                                                              const void* q_gate, uint16_t* gated_out,
                                                              uint64_t wait_ns) {
   pdl_wait_primary();
+  // the next kernel may set up now; it reads nothing before this one completes
+  pdl_launch_dependents();
   const XchgDev& x = *xp;
   const int mh = blockIdx.x;
   const int m = mh / QH, h = mh % QH, d = threadIdx.x, kvh = h / GQA;
