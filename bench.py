@@ -613,7 +613,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode32k", choices=["decode32k", "batched", "longctx"])
+    ap.add_argument("--workload", default="decode32k", choices=["decode32k", "batched", "longctx", "qmv", "gdn"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--decode-only", action="store_true", help="skip the batched / longctx blocks")
     ap.add_argument("--rows", type=int, default=1, choices=[1, 3], help="rows of --workload longctx")
@@ -656,6 +656,16 @@ def main():
                         "per_gpu_kv_bytes": r["per_gpu_bytes_max"]})
         return blk
 
+    if args.workload in ("qmv", "gdn"):
+        us, nbytes = (bench_qmv if args.workload == "qmv" else bench_gdn)(args, world)
+        gbs = nbytes / (us * 1e-6) / 1e9
+        if rank == 0:
+            emit({"metric": METRIC, "value": round(us, 3), "unit": "µs/launch", "n_gpus": world, "steps": args.steps,
+                  "warmup": args.warmup, "higher_is_better": False, "dtype": "f32", "data": "synthetic",
+                  "config": {"workload": args.workload},
+                  "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                               "frac": round(gbs / pk["hbm_gbs"], 4), "algorithmic_bytes": nbytes}})
+        return
     if args.workload in ("batched", "longctx"):
         r = bench_batched(args, rank, world, local) if args.workload == "batched" else \
             bench_longctx(args, rank, world, local, rows=args.rows)
