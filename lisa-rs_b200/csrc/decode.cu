@@ -278,6 +278,9 @@ __global__ void __launch_bounds__(32 * (4 * ROWS + 1), 1)
     DEC_TRACE(0);
     if (!mbar_wait(&full[s], (it / DEC_STAGES) & 1, p.err, ERR_TIMEOUT_FULL, p.wait_ns)) return;
     DEC_TRACE(1);
+#ifdef LISA_DECODE_TRACE
+    if (it == 0 && threadIdx.x == 0) p.trace[16 + blockIdx.x * 4 + 3] = global_timer_ns();
+#endif
     const int code = slot_code[s];
     if (code < 0) break;
     const uint32_t cur_chunk = (uint32_t)code >> 8, cur_tile = (uint32_t)code & 0xffu;
@@ -468,6 +471,9 @@ __device__ __forceinline__ void lse_fold(float& m, float& a, float& d, float cm,
 
 __global__ void __launch_bounds__(CMB_THREADS) decode_combine_kernel(const DecodeParams p) {
   pdl_wait_primary();
+#ifdef LISA_DECODE_TRACE
+  if (threadIdx.x == 0) atomicMin(&p.trace[10], (unsigned long long)global_timer_ns());
+#endif
   pdl_launch_dependents();
   if (blockIdx.x == 0 && threadIdx.x < KVH) p.sched[threadIdx.x] = 0;  // ready for the next launch
   __shared__ Lse2 s_state[CMB_PHASES][32];
@@ -518,6 +524,9 @@ __global__ void __launch_bounds__(CMB_THREADS) decode_combine_kernel(const Decod
     }
     __syncthreads();
   }
+#ifdef LISA_DECODE_TRACE
+  if (threadIdx.x == 0) atomicMax(&p.trace[11], (unsigned long long)global_timer_ns());
+#endif
   if (phase != 0) return;
   if (p.xchg) {
     // Exchange mode: this CTA's slice of the window partial (row m, kv head,
@@ -683,9 +692,16 @@ static cudaError_t launch_split(const DecodeParams& p, const CUtensorMap& tk, co
   return cudaLaunchKernelEx(&cfg, decode_split_kernel<ROWS>, tk, tv, p);
 }
 
+#ifdef LISA_DECODE_TRACE
+unsigned long long* g_decode_trace = nullptr;  // debug builds: set by a trace harness
+#endif
+
 cudaError_t launch_decode(const DecodeParams& p_in, int rows, const CUtensorMap& tk, const CUtensorMap& tv,
                           int num_sms, cudaStream_t stream) {
   DecodeParams p = p_in;
+#ifdef LISA_DECODE_TRACE
+  p.trace = g_decode_trace;
+#endif
   // inverse frequencies once per process; cos/sin of the f32 angle in double,
   // for the rows of this call only (host time is part of every layer call)
   static const struct InvFreqTable {

@@ -10,7 +10,10 @@ namespace lisa {
 // over the chunk's 64-token stages in order and the chunk partials are merged
 // in a fixed order. Chunk boundaries depend only on the token index, so a
 // verify row gives bit-identical results to the same row decoded alone.
-constexpr int DEC_CHUNK = 448;  // tokens per chunk
+#ifndef LISA_DEC_CHUNK
+#define LISA_DEC_CHUNK 448
+#endif
+constexpr int DEC_CHUNK = LISA_DEC_CHUNK;  // tokens per chunk (a multiple of DEC_TILE)
 constexpr int DEC_TILE = 64;    // tokens per pipeline stage (4 warps x 16)
 constexpr int DEC_STAGES = 3;   // TMA ring depth per CTA
 constexpr int DEC_STAGE_BYTES = 2 * DEC_TILE * 256 * 2;  // K + V stage, 64 KB
