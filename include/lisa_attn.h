@@ -222,9 +222,10 @@ int lisa_attn_batch_check_device_error(lisa_attn_batch* b, void* stream);
  * of one node, world <= 8). Per step every rank runs lisa_attn_xchg_decode on
  * its window with the same inputs: the split kernel streams the window, the
  * combine kernel writes the window's per-(row, head) partial (normalised O,
- * max, sum) into every rank's receive region with peer stores and raises
- * release flags there, and a merge kernel waits (bounded) for all ranks'
- * flags, merges the partials by log-sum-exp in rank order and applies the
+ * max, sum) into every rank's receive region with peer stores, every value in
+ * an 8-byte word tagged with the step number, and a merge kernel waits
+ * (bounded) until the words it needs carry the step, merges the partials by
+ * log-sum-exp in rank order and applies the
  * gate, so every rank ends with the same gated_out. The merge of
  * sdpa_decode_final (attention.metal:611-641), taken across GPUs.
  * Setup: every rank calls lisa_attn_xchg_create, exports its receive region

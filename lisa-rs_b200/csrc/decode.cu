@@ -531,10 +531,13 @@ __global__ void __launch_bounds__(CMB_THREADS) decode_combine_kernel(const Decod
   if (p.xchg) {
     // Exchange mode: this CTA's slice of the window partial (row m, kv head,
     // 8 dims, 6 heads) goes to every rank's receive region (peer stores over
-    // NVLink), then one release flag per destination says it is there.
+    // NVLink). Every value travels with the step number in one aligned 8-byte
+    // store (value bits low, step high), so a reader that sees the step in a
+    // word has that word's value: no flag and no fence.
     const XchgDev& x = *p.xchg;
     const uint32_t epoch = x.state[0] + 1;
     const size_t xs = (size_t)(epoch & 1) * x.world + x.rank;  // parity, source rank
+    const uint64_t tag = (uint64_t)epoch << 32;
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const int hl = 2 * hp + e;
@@ -544,21 +547,13 @@ __global__ void __launch_bounds__(CMB_THREADS) decode_combine_kernel(const Decod
       const float o = nch ? a / dn : 0.f;
       const size_t rec = ((xs * x.max_rows + m) * QH + h) * XCHG_REC;
       for (int dst = 0; dst < x.world; ++dst) {
-        float* r = x.recv[dst] + rec;
-        r[dim] = o;
+        uint64_t* r = x.recv[dst] + rec;
+        st_relaxed_sys_u64(r + dim, tag | __float_as_uint(o));
         if (dim == 0) {
-          r[HD] = nch ? gmax : -INFINITY;
-          r[HD + 1] = nch ? dn : 0.f;
+          st_relaxed_sys_u64(r + HD, tag | __float_as_uint(nch ? gmax : -INFINITY));
+          st_relaxed_sys_u64(r + HD + 1, tag | __float_as_uint(nch ? dn : 0.f));
         }
       }
-    }
-    // The warp barrier orders every lane's peer stores before lane 0's
-    // release store of the flag (release is cumulative at system scope), so
-    // no separate fence is needed.
-    __syncwarp();
-    if (slot == 0) {
-      const size_t f = (((size_t)x.rank * 3 + m) * KVH + kvh) * 32 + db;
-      for (int dst = 0; dst < x.world; ++dst) st_release_sys(x.flags[dst] + f, epoch);
     }
     return;
   }
@@ -608,8 +603,8 @@ __global__ void __launch_bounds__(256) merge_windows_kernel(int n_parts, int row
 }
 
 // Exchange merge: grid rows * 24 CTAs (row m, head h) of 256 threads (one per
-// dim). Threads 0 .. 32*world-1 wait (bounded, acquire loads at system scope)
-// for the flags of the 32 dim blocks of kv head h/6 from every rank; then the
+// dim). Thread d waits (bounded) until its dim and the (max, sum) words of
+// every rank's record carry this step; then the
 // world partials are merged by log-sum-exp in rank order (the same order on
 // every rank, so every rank produces identical bits) and gated. The last CTA
 // to finish advances the step counter.
@@ -623,37 +618,38 @@ __global__ void __launch_bounds__(256) merge_exchange_kernel(const XchgDev* xp, 
   const int mh = blockIdx.x;
   const int m = mh / QH, h = mh % QH, d = threadIdx.x, kvh = h / GQA;
   const uint32_t epoch = x.state[0] + 1;
-  __shared__ int s_fail;
-  if (threadIdx.x == 0) s_fail = 0;
-  __syncthreads();
-  if (threadIdx.x < 32 * x.world) {
-    const int src = threadIdx.x >> 5, db = threadIdx.x & 31;
-    const uint32_t* f = x.flags[x.rank] + (((size_t)src * 3 + m) * KVH + kvh) * 32 + db;
-    if ((int32_t)(ld_acquire_sys(f) - epoch) < 0) {
-      const uint64_t t0 = global_timer_ns();
-      while ((int32_t)(ld_acquire_sys(f) - epoch) < 0) {
-        if (global_timer_ns() - t0 > wait_ns) {
-          atomicExch(reinterpret_cast<int*>(x.state + 2), ERR_TIMEOUT_XCHG);
-          s_fail = 1;
-          break;
-        }
-        __nanosleep(64);
+  const uint64_t* base = x.recv[x.rank] + (size_t)(epoch & 1) * x.world * x.max_rows * QH * XCHG_REC;
+  // the value of word w of source g's record, once it carries this step
+  const uint64_t t0 = global_timer_ns();
+  bool fail = false;
+  auto take = [&](int g, int w) -> float {
+    const uint64_t* a = base + (((size_t)g * x.max_rows + m) * QH + h) * XCHG_REC + w;
+    uint64_t v = ld_relaxed_sys_u64(a);
+    while ((uint32_t)(v >> 32) != epoch && !fail) {
+      if (global_timer_ns() - t0 > wait_ns) {
+        atomicExch(reinterpret_cast<int*>(x.state + 2), ERR_TIMEOUT_XCHG);
+        fail = true;
+        break;
       }
+      __nanosleep(32);
+      v = ld_relaxed_sys_u64(a);
     }
+    return __uint_as_float((uint32_t)v);
+  };
+  float mg[XCHG_MAX_WORLD], lgv[XCHG_MAX_WORLD], og[XCHG_MAX_WORLD];
+  float gmax = -INFINITY;
+  for (int g = 0; g < x.world; ++g) {
+    mg[g] = take(g, HD);
+    lgv[g] = take(g, HD + 1);
+    og[g] = take(g, d);
+    gmax = fmaxf(gmax, mg[g]);
   }
-  __syncthreads();
-  if (!s_fail) {
-    const float* base = x.recv[x.rank] + (size_t)(epoch & 1) * x.world * x.max_rows * QH * XCHG_REC;
-    float gmax = -INFINITY;
-    for (int g = 0; g < x.world; ++g)
-      gmax = fmaxf(gmax, __ldcv(base + (((size_t)g * x.max_rows + m) * QH + h) * XCHG_REC + HD));
+  if (!fail) {
     float acc = 0.f, den = 0.f;
     for (int g = 0; g < x.world; ++g) {
-      const float* r = base + (((size_t)g * x.max_rows + m) * QH + h) * XCHG_REC;
-      const float lg = __ldcv(r + HD + 1);
-      if (lg == 0.f) continue;
-      const float w = exp2f(LOG2E * (__ldcv(r + HD) - gmax)) * lg;
-      acc += w * __ldcv(r + d);
+      if (lgv[g] == 0.f) continue;
+      const float w = exp2f(LOG2E * (mg[g] - gmax)) * lgv[g];
+      acc += w * og[g];
       den += w;
     }
     const float o = den > 0.f ? acc / den : 0.f;

@@ -32,18 +32,16 @@ constexpr int HD_FLOATS_PLUS_ML = 256 + 2;
 // Window-partial exchange between the ranks of one split-KV sequence (one
 // GPU per rank, peer memory mapped by CUDA IPC). Lives in device memory.
 constexpr int XCHG_MAX_WORLD = 8;
-constexpr int XCHG_REC = HD_FLOATS_PLUS_ML;  // floats per (row, head) record: O[256], max, sum
+constexpr int XCHG_REC = HD_FLOATS_PLUS_ML;  // words per (row, head) record: O[256], max, sum
 struct XchgDev {
-  float* recv[XCHG_MAX_WORLD];      // receive region of rank i, as mapped in this process
-  uint32_t* flags[XCHG_MAX_WORLD];  // flag array of rank i, as mapped in this process
+  uint64_t* recv[XCHG_MAX_WORLD];   // receive region of rank i, as mapped in this process
   uint32_t* state;                  // this rank: [0] completed exchanges, [1] merge CTAs done, [2] error word
   int world, rank, max_rows;
 };
-// recv[parity][src rank][row][24 heads][XCHG_REC] floats; flags[src][row][kv head][32 dim blocks]
-__host__ __device__ constexpr size_t xchg_recv_floats(int world, int max_rows) {
+// recv[parity][src rank][row][24 heads][XCHG_REC] words: value bits | step << 32
+__host__ __device__ constexpr size_t xchg_recv_words(int world, int max_rows) {
   return (size_t)2 * world * max_rows * 24 * XCHG_REC;
 }
-__host__ __device__ constexpr size_t xchg_flag_words(int world) { return (size_t)world * 3 * 4 * 32; }
 
 struct DecodeParams {
   const void* q_gate;  // [rows][24][512]

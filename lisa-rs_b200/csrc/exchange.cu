@@ -8,17 +8,20 @@
 //                          window owns them), chunk partials to the workspace
 //   decode_combine_kernel  folds the chunks into one window partial per
 //                          (row, head) and stores it straight into every
-//                          rank's receive region (peer stores), then raises one
-//                          release flag per (source, row, kv head, dim block)
-//                          on every rank
-//   merge_exchange_kernel  waits (bounded) for all ranks' flags, merges the
-//                          partials by log-sum-exp in rank order and applies
-//                          the sigmoid gate
+//                          rank's receive region (peer stores), each value in
+//                          one 8-byte word with the step number beside it
+//   merge_exchange_kernel  waits (bounded) until the words it needs from every
+//                          rank carry this step, merges the partials by
+//                          log-sum-exp in rank order and applies the gate
+// Tagging every word with its step (the low-latency protocol of collective
+// libraries) needs neither a flag nor a memory fence: an aligned 8-byte store
+// is seen whole or not at all. A first version that published one flag per
+// block after the data saw stale data on 4 GPUs once the fences were removed.
 // Receive regions are double-buffered by step parity: a rank can only publish
 // step e+2 after finishing step e+1, which needed every rank's step-e+1
 // partials, which each rank published after finishing its step-e merge; so
 // the parity-e data a slow rank is still reading is never overwritten.
-// Flags hold the step number (monotonic), so they are never reset. The step
+// Words hold the step number, so the region is never cleared. The step
 // counter lives on the device (advanced by the merge kernel), so a step can be
 // captured in a CUDA graph and replayed.
 //
@@ -43,7 +46,7 @@ struct lisa_attn_xchg {
   int rank = 0;
   int max_rows = 3;
   uint32_t window_rows = 0;
-  uint8_t* region = nullptr;     // [flags (padded to 4 KB)][recv], exported by IPC
+  uint8_t* region = nullptr;     // receive region (tagged words), exported by IPC
   size_t region_bytes = 0;
   uint32_t* state = nullptr;     // local only: step counter, merge CTAs done, error word
   XchgDev* dev = nullptr;        // device copy of the peer table
@@ -55,7 +58,6 @@ struct lisa_attn_xchg {
 
 namespace {
 
-constexpr size_t FLAG_BYTES_PAD = 4096;
 
 struct DevGuard {
   int prev = -1;
@@ -100,7 +102,7 @@ int lisa_attn_xchg_create(int device, int world, int rank, int max_rows, uint32_
   x->rank = rank;
   x->max_rows = max_rows;
   x->window_rows = window_rows;
-  x->region_bytes = FLAG_BYTES_PAD + xchg_recv_floats(world, max_rows) * sizeof(float);
+  x->region_bytes = xchg_recv_words(world, max_rows) * sizeof(uint64_t);
   x->workspace_bytes = lisa_attn_window_workspace_bytes(window_rows, max_rows);
   bool ok = cudaMalloc(&x->region, x->region_bytes) == cudaSuccess &&
             cudaMalloc(&x->state, 256) == cudaSuccess && cudaMalloc(&x->dev, sizeof(XchgDev)) == cudaSuccess &&
@@ -146,8 +148,7 @@ int lisa_attn_xchg_open(lisa_attn_xchg* x, const void* handles) {
       x->peer_base[i] = p;
       base = static_cast<uint8_t*>(p);
     }
-    d.flags[i] = reinterpret_cast<uint32_t*>(base);
-    d.recv[i] = reinterpret_cast<float*>(base + FLAG_BYTES_PAD);
+    d.recv[i] = reinterpret_cast<uint64_t*>(base);
   }
   if (cudaMemcpy(x->dev, &d, sizeof(d), cudaMemcpyHostToDevice) != cudaSuccess) return LISA_ECUDA;
   x->opened = true;
