@@ -487,6 +487,21 @@ __global__ void __launch_bounds__(CMB_THREADS) decode_combine_kernel(const Decod
   const int64_t lim64 = (int64_t)p.base + m + 1 - (int64_t)p.kv_lo;
   const uint32_t lim = lim64 <= 0 ? 0u : (uint32_t)(lim64 < (int64_t)p.extent ? lim64 : (int64_t)p.extent);
   const uint32_t nch = (lim + DEC_CHUNK - 1) / DEC_CHUNK;
+  // the gate of this thread's two heads, loaded now so that its latency
+  // overlaps the partials' (phase 0 applies it at the end)
+  float sig[2] = {0.f, 0.f};
+  if (phase == 0 && p.gated_out) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int hl = 2 * hp + e;
+      if (hl < GQA) {
+        // gate_out_bf16 (attention.metal:520-531); gate = bf16-rounded raw gate
+        const float gv = load_in_bf16(p.q_gate, (size_t)m * QROW + (size_t)(kvh * GQA + hl) * 512 + 256 + dim,
+                                      p.in_bf16);
+        sig[e] = 1.0f / (1.0f + exp2f(-LOG2E * gv));
+      }
+    }
+  }
   const size_t unit0 = ((size_t)m * KVH + kvh) * p.chunk_cap;
 
   Lse2 st = {-INFINITY, -INFINITY, 0.f, 0.f, 0.f, 0.f};
@@ -565,10 +580,7 @@ __global__ void __launch_bounds__(CMB_THREADS) decode_combine_kernel(const Decod
     const float a = e ? st.a1 : st.a0, dn = e ? st.d1 : st.d0, gmax = e ? st.m1 : st.m0;
     const float o = nch ? a / dn : 0.f;
     if (p.gated_out) {
-      // gate_out_bf16 (attention.metal:520-531); gate = bf16-rounded raw gate
-      const float gv = load_in_bf16(p.q_gate, (size_t)m * QROW + (size_t)h * 512 + 256 + dim, p.in_bf16);
-      const float sg = 1.0f / (1.0f + exp2f(-LOG2E * gv));
-      p.gated_out[(size_t)m * OROW + h * HD + dim] = f32_to_bf16_bits(o * sg);
+      p.gated_out[(size_t)m * OROW + h * HD + dim] = f32_to_bf16_bits(o * sig[e]);
     } else {
       p.win_o[((size_t)m * QH + h) * HD + dim] = o;
       if (dim == 0) {
