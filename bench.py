@@ -44,6 +44,8 @@ LAYERS = 16
 CTX = 32768
 PREFILL_TOKENS, PREFILL_CHUNK = 4096, 512
 PREFILL_FLOP = 4 * QH * HD * sum(range(1, PREFILL_TOKENS + 1))  # causal-exact QK^T + PV
+DEEP_BASE = 16384  # the deep-chunk line: one 512-row chunk at this base
+DEEP_FLOP = 4 * QH * HD * sum(range(DEEP_BASE + 1, DEEP_BASE + PREFILL_CHUNK + 1))
 # DRAM bytes of one decode layer call at ctx 32768 (split kernel read 134.30 MB
 # + write 3.46 MB, combine read 2.49 MB), from an ncu capture
 # (dram__bytes_read.sum + dram__bytes_write.sum) of both kernels.
@@ -344,7 +346,28 @@ def bench_prefill(args, world):
     ms = timed(graph.replay, args.steps, args.warmup, world, stream)
     ms_eager = timed(step_eager, args.steps, args.warmup, world, stream)
     runner.check_device_error()
-    return ms, ms_eager
+
+    # One 512-row chunk deep into the context (base 16384 over a filled
+    # cache), captured once with the planner's grid (which splits its units
+    # into two key ranges) and once with splitting off.
+    deep = lisa_attn.AttnRunner(1, DEEP_BASE + PREFILL_CHUNK)
+    kc, vc = deep.kv_cache(0)
+    kc.copy_(torch.randn(kc.shape, generator=gen, device="cuda").to(torch.bfloat16))
+    vc.copy_(torch.randn(vc.shape, generator=gen, device="cuda").to(torch.bfloat16))
+    lib = lisa_attn.load_library()
+    deep_ms = {}
+    for name, mode in (("auto", 0), ("never", 1)):
+        prev = lib.lisa_attn_debug_prefill_split(mode)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(cap):
+            with torch.cuda.graph(g, stream=cap):
+                deep.prefill_layer(0, DEEP_BASE, PREFILL_CHUNK, q[:PREFILL_CHUNK], k[:PREFILL_CHUNK],
+                                   v[:PREFILL_CHUNK], w, out[:PREFILL_CHUNK], cap)
+        lib.lisa_attn_debug_prefill_split(prev)
+        torch.cuda.synchronize()
+        deep_ms[name] = timed(g.replay, args.steps, args.warmup, world, stream) / args.steps
+    deep.check_device_error()
+    return ms, ms_eager, deep_ms
 
 
 def cpu_baseline_decode(seconds: float = 8.0, threads: int | None = None):
@@ -686,7 +709,7 @@ def main():
 
     r = bench_decode32k(args, rank, world, local)
     torch.cuda.empty_cache()
-    pf_ms, pf_ms_eager = bench_prefill(args, world)
+    pf_ms, pf_ms_eager, deep_ms = bench_prefill(args, world)
     torch.cuda.empty_cache()
     qmv_us, qmv_bytes = bench_qmv(args, world)
     gdn_us, gdn_bytes = bench_gdn(args, world)
@@ -749,7 +772,14 @@ def main():
                     "roofline": {"bound": "tensor", "achieved": round(pf_tflops, 2), "peak": pk["bf16_tflops"],
                                  "unit": "TFLOP/s", "frac": round(pf_tflops / pk["bf16_tflops"], 4), "traffic": None,
                                  "kernel": "prefill_prologue_kernel + prefill_attn_kernel, 8 chunk calls"},
-                    "gpu_launches_per_step": 2 * (PREFILL_TOKENS // PREFILL_CHUNK)},
+                    "gpu_launches_per_step": 2 * (PREFILL_TOKENS // PREFILL_CHUNK),
+                    "deep_chunk": {"workload": f"one 512-row chunk at base {DEEP_BASE} over a filled cache, "
+                                               "CUDA graph; grid as planned (key ranges split) and unsplit",
+                                   "ms": round(deep_ms["auto"], 4), "ms_unsplit": round(deep_ms["never"], 4),
+                                   "tflops": round(DEEP_FLOP / (deep_ms["auto"] * 1e-3) / 1e12, 2),
+                                   "tflops_unsplit": round(DEEP_FLOP / (deep_ms["never"] * 1e-3) / 1e12, 2),
+                                   "frac_burst": round(DEEP_FLOP / (deep_ms["auto"] * 1e-3) / 1e12
+                                                       / pk["bf16_tflops"], 4)}},
     }
     qmv_gbs = qmv_bytes / (qmv_us * 1e-6) / 1e9
     line["qmv"] = {"workload": "fused q/k/v affine-u4 QMV of one decode step (lisa_attn_qmv_u4, M=1, 5120 -> "

@@ -296,6 +296,19 @@ int lisa_attn_noalloc_check_device_error(void);
  * withhold_loads without a limit or a limit above 10 s. */
 int lisa_attn_debug_wait_fault(uint32_t wait_limit_us, int withhold_loads);
 
+/* Test and measurement hook for the prefill attention grid; no lisa-rs
+ * counterpart. A prefill chunk's (query row pair, head) units may each be split
+ * into two consecutive key ranges that run as separate clusters and merge
+ * their partial results (used when a cost model of the dispatch predicts at
+ * least 10 % less time, i.e. for chunks deep into the context). mode:
+ * LISA_PREFILL_SPLIT_AUTO (default), _NEVER, or _ALWAYS (every unit that can
+ * be split, at 70 % of its keys, whatever the model says). Process-wide;
+ * returns the previous mode, or LISA_EINVAL for an unknown mode. */
+#define LISA_PREFILL_SPLIT_AUTO 0
+#define LISA_PREFILL_SPLIT_NEVER 1
+#define LISA_PREFILL_SPLIT_ALWAYS 2
+int lisa_attn_debug_prefill_split(int mode);
+
 /* ---- affine-u4 projections (QMV) --------------------------------------------
  * The quantised matrix-vector products around the attention layer for the
  * decode (rows = 1) and verify (rows = 3) shapes: q4_qmv_fast / fused2/3/4

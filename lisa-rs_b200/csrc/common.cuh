@@ -31,6 +31,7 @@ constexpr int ERR_TIMEOUT_FULL = 1;
 constexpr int ERR_TIMEOUT_EMPTY = 2;
 constexpr int ERR_TIMEOUT_MMA = 3;
 constexpr int ERR_TIMEOUT_XCHG = 4;  // a peer's partials did not arrive
+constexpr int ERR_TIMEOUT_MERGE = 5;  // a split prefill unit's first partial did not arrive
 
 // Bounded waits give up after this many nanoseconds of %globaltimer.
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;

@@ -29,8 +29,14 @@
 //                O/l * sigmoid(gate) staged in shared memory and written by
 //                one TMA store.
 // Key tiles past the pair's last query row are skipped (causal tile skipping).
+// For chunks deep into the context the host planner (plan_segments) splits
+// every (pair, head) unit into two key ranges run by separate clusters, so
+// that the grid fills the SMs that 48 units leave idle; the two ranges merge
+// through a global partial (ticket + flag per CTA rank).
 #include <algorithm>
+#include <atomic>
 
+#include "../../include/lisa_attn.h"
 #include "common.cuh"
 #include "prefill.cuh"
 #include "dispatch.h"
@@ -204,9 +210,12 @@ __global__ void __launch_bounds__(256, 4) prefill_prologue_kernel(const PrefillP
 #endif
 }
 
-// Grid: clusters of 2 CTAs, n_pairs * 24 clusters, heaviest (last) query
-// row pairs first. Cluster rank 0 holds query rows [256 qp, 256 qp + 128),
-// rank 1 the next 128.
+// Grid: clusters of 2 CTAs, one per key-range segment of p.seg_*: a (query
+// row pair, head) unit whole, or one of the two consecutive key ranges of a
+// split unit. Cluster rank 0 holds query rows [256 qp, 256 qp + 128), rank 1
+// the next 128. The two segments of a split unit merge through p.part: per
+// CTA rank, the first to finish stores its unnormalised O, running max and
+// sum, the second folds them into its own and writes the gated output.
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
     prefill_attn_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                         const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tg,
@@ -220,15 +229,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
-  const int n_qt = (p.rows + PF_BM - 1) / PF_BM;
-  const int n_pairs = (n_qt + 1) / 2;
   const int cl = (int)(blockIdx.x >> 1);
-  const int qp = n_pairs - 1 - cl / QH;
-  const int h = cl % QH, kvh = h / GQA;
+  const uint32_t su = p.seg_unit[cl];
+  const int h = (int)(su & 0xffu), qp = (int)((su >> 8) & 0xfu), kvh = h / GQA;
+  const bool split = (su >> 12) & 1u;
   const int r0 = qp * 2 * PF_BM + (int)rank * PF_BM;
-  const int pair_end = min(qp * 2 * PF_BM + 2 * PF_BM, p.rows);
-  const uint32_t kv_end = p.base + (uint32_t)pair_end;  // keys [0, kv_end) for both CTAs
-  const int n_tiles = (int)((kv_end + PF_BN - 1) / PF_BN);
+  // key tiles [t_lo, t_lo + n_tiles); loop indices below are relative to t_lo
+  const uint32_t t_lo = p.seg_lo[cl];
+  const int n_tiles = (int)(p.seg_hi[cl] - t_lo);
+  const int slot = (qp * QH + h) * 2 + (int)rank;  // split partial / ticket slot
 
 #ifdef LISA_PREFILL_TRACE
   if (threadIdx.x == 0) p.trace[64 + blockIdx.x * 8 + 0] = global_timer_ns();
@@ -256,7 +265,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
   // only after it has completed. The K/V producers first issue the loads of
   // the first two key tiles when they hold only positions below `base`
   // (written by earlier calls), then wait too.
-  const int n_early = min(min(2, n_tiles), (int)(p.base / PF_BN));
+  const int n_early = min(min(2, n_tiles), max(0, (int)(p.base / PF_BN) - (int)t_lo));
   if (!((warp == 0 || warp == 2) && lane == 0)) pdl_wait_primary();
   pdl_launch_dependents();
 #ifdef LISA_PREFILL_TRACE
@@ -290,7 +299,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
       const int s = j & 1;
       if (rank == 0) mbar_arrive_expect_tx(&bars[B_KFULL + s], 2 * PF_KH_BYTES);
       tma_load_4d_pair(smem + PF_OFF_K + s * PF_KH_BYTES, &tk, lead_bar(B_KFULL + s), 0,
-                       j * PF_BN + (int)rank * (PF_BN / 2), 0, kvh);
+                       ((int)t_lo + j) * PF_BN + (int)rank * (PF_BN / 2), 0, kvh);
     };
     for (int j = 0; j < n_early; ++j) load_k(j);
     pdl_wait_primary();
@@ -317,8 +326,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
     auto load_v = [&](int j) {
       const int s = j & 1;
       if (rank == 0) mbar_arrive_expect_tx(&bars[B_VFULL + s], 2 * PF_VH_BYTES);
-      tma_load_4d_pair(smem + PF_OFF_V + s * PF_VH_BYTES, &tv, lead_bar(B_VFULL + s), 0, j * PF_BN,
-                       2 * (int)rank, kvh);
+      tma_load_4d_pair(smem + PF_OFF_V + s * PF_VH_BYTES, &tv, lead_bar(B_VFULL + s), 0,
+                       ((int)t_lo + j) * PF_BN, 2 * (int)rank, kvh);
     };
     for (int j = 0; j < n_early; ++j) load_v(j);
     pdl_wait_primary();
@@ -440,7 +449,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
       float x[64];  // raw scores Q.K (unscaled)
 #pragma unroll
       for (int c = 0; c < 64; ++c) x[c] = __uint_as_float(c < 32 ? sa[c] : sb[c - 32]);
-      const uint32_t key0 = (uint32_t)j * PF_BN + half * 64;
+      const uint32_t key0 = (t_lo + (uint32_t)j) * PF_BN + half * 64;
       if (key0 + 63 > pos_row) {  // diagonal tile: keys past this row's position
 #pragma unroll
         for (int c = 0; c < 64; ++c)
@@ -544,10 +553,84 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
     // Sum the two halves' denominators (half 0 + half 1).
     xsum[half * PF_BM + row] = l;
     named_bar_sync(2 + wi, 64);
-    const float l_row = xsum[row] + xsum[PF_BM + row];
+    float l_row = xsum[row] + xsum[PF_BM + row];
     if (p.in_bf16) ok = ok && mbar_wait(&bars[B_G], 0, p.err, ERR_TIMEOUT_FULL);
+#ifdef LISA_PREFILL_TRACE
+    if (threadIdx.x == 128) p.trace[64 + blockIdx.x * 8 + 5] = global_timer_ns();
+#endif
+    // Split unit: the first segment to get here stores its partial and
+    // leaves; the second merges it. Both scale by 2^(m_seg - max(m_a, m_b)),
+    // a formula symmetric in the two segments, so the result does not depend
+    // on which finished first.
+    float a_own = 1.f, a_oth = 0.f;
+    const float4* oth = nullptr;
+    if (split) {
+      uint32_t* ticket = p.tickets + slot;
+      uint32_t* ready = p.tickets + 2 * PF_MAX_UNITS + slot;
+      float4* po = reinterpret_cast<float4*>(p.part + (size_t)slot * (PF_BM * HD));
+      float* pml = p.part + (size_t)2 * PF_MAX_UNITS * PF_BM * HD + (size_t)slot * 2 * PF_BM;
+      int* tk_sh = reinterpret_cast<int*>(smem + PF_OFF_BAR + 512);
+      if (threadIdx.x == 128) *tk_sh = (int)atomicAdd(ticket, 1u);
+      named_bar_sync(6, 256);
+      const bool first = *tk_sh == 0;
+      if (first) {
+        if (ok) {
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < HD / 64; ++c) {
+            const int col = half * (HD / 2) + c * 32;
+            uint32_t ov[32];
+            tmem_ld32(lane_addr + PF_TMEM_O + col, ov);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 8; ++i)  // layout [dim/4][row][4]: a warp stores 512 contiguous bytes
+              __stcg(po + (col / 4 + i) * PF_BM + row,
+                     make_float4(__uint_as_float(ov[4 * i]), __uint_as_float(ov[4 * i + 1]),
+                                 __uint_as_float(ov[4 * i + 2]), __uint_as_float(ov[4 * i + 3])));
+          }
+          if (half == 0) {
+            __stcg(pml + row, mr);
+            __stcg(pml + PF_BM + row, l_row);
+          }
+        }
+        __threadfence();
+        named_bar_sync(6, 256);
+        if (threadIdx.x == 128) st_release_gpu(ready, 1u);
+        ok = false;  // no output from this segment
+      } else {
+        if (threadIdx.x == 128) {
+          // the first segment has passed its ticket: its store is in flight
+          const uint64_t t0 = global_timer_ns();
+          bool got = true;
+          while (ld_acquire_gpu(ready) == 0u) {
+            if (global_timer_ns() - t0 > WAIT_LIMIT_NS) {
+              atomicExch(p.err, ERR_TIMEOUT_MERGE);
+              got = false;
+              break;
+            }
+          }
+          *tk_sh = got ? 1 : -1;
+          // ready for the next launch (stream-ordered after this one)
+          *ticket = 0u;
+          *ready = 0u;
+        }
+        named_bar_sync(6, 256);
+        ok = ok && *tk_sh == 1;
+        const float m_oth = __ldcg(pml + row);
+        const float m = fmaxf(mr, m_oth);
+        a_own = fast_exp2((mr - m) * kLog2Scale);
+        a_oth = fast_exp2((m_oth - m) * kLog2Scale);
+        l_row = __fadd_rn(__fmul_rn(l_row, a_own), __fmul_rn(__ldcg(pml + PF_BM + row), a_oth));
+        oth = po;
+      }
+    }
     // gated rows staged in the (now idle) V ring as [group][row][64] with the
     // 128-byte swizzle, then written by one TMA store (rows >= p.rows clipped)
+#ifdef LISA_PREFILL_TRACE
+    if (threadIdx.x == 128) p.trace[64 + blockIdx.x * 8 + 6] = global_timer_ns();
+#endif
+    // no contraction into an FMA: keeps the merge symmetric in its two terms
+    auto mix = [&](float own, float other) { return __fadd_rn(__fmul_rn(own, a_own), __fmul_rn(other, a_oth)); };
     uint8_t* stage = smem + PF_OFF_V;
     const uint8_t* gtile = smem + PF_OFF_K;
     if (ok) {
@@ -559,6 +642,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
         const int grp = col >> 6, ch0 = (col & 63) >> 3;
         uint32_t ov[32];
         tmem_ld32(lane_addr + PF_TMEM_O + col, ov);
+        float4 ot[8];
+        if (oth) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) ot[i] = __ldcg(oth + (col / 4 + i) * PF_BM + row);
+        }
         uint32_t gw[16];
         if (p.in_bf16) {
 #pragma unroll
@@ -572,6 +660,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
           for (int i = 0; i < 16; ++i) gw[i] = gpk[c * 16 + i];
         }
         tmem_wait_ld();
+        if (oth) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            ov[4 * i] = __float_as_uint(mix(__uint_as_float(ov[4 * i]), ot[i].x));
+            ov[4 * i + 1] = __float_as_uint(mix(__uint_as_float(ov[4 * i + 1]), ot[i].y));
+            ov[4 * i + 2] = __float_as_uint(mix(__uint_as_float(ov[4 * i + 2]), ot[i].z));
+            ov[4 * i + 3] = __float_as_uint(mix(__uint_as_float(ov[4 * i + 3]), ot[i].w));
+          }
+        }
         uint32_t outw[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
@@ -585,6 +682,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
               make_uint4(outw[4 * i], outw[4 * i + 1], outw[4 * i + 2], outw[4 * i + 3]);
       }
     }
+#ifdef LISA_PREFILL_TRACE
+    if (threadIdx.x == 128) p.trace[64 + blockIdx.x * 8 + 7] = global_timer_ns();
+#endif
     fence_proxy_async_smem();
     named_bar_sync(6, 256);  // the staged tile is complete
     if (ok && threadIdx.x == 128) {
@@ -609,12 +709,134 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
   }
 }
 
-size_t prefill_workspace_bytes() { return (size_t)QH * PF_MAX_ROWS * HD * sizeof(uint16_t); }
+namespace {
+constexpr size_t PF_QWS_BYTES = (size_t)QH * PF_MAX_ROWS * HD * sizeof(uint16_t);
+// partials: O per (unit, rank) then (max, sum) per row
+constexpr size_t PF_PART_BYTES = (size_t)2 * PF_MAX_UNITS * (PF_BM * HD + 2 * PF_BM) * sizeof(float);
+constexpr size_t PF_TICKET_BYTES = (size_t)2 * 2 * PF_MAX_UNITS * sizeof(uint32_t);
+
+// Cost model of the segment planner, in key-tile times (about 1.45 us each
+// with 96 busy SMs), fitted to a globaltimer trace of the config-2 chunks: a
+// cluster's fixed cost (start, pipeline fill, epilogue), the extra cost of a
+// split segment (storing or loading its partial), and the slower tiles when
+// the split grid keeps every SM busy (shared L2 and TMA traffic).
+constexpr float PF_PLAN_FIXED = 4.5f;
+constexpr float PF_PLAN_SPLIT = 1.5f;
+constexpr float PF_PLAN_BUSY = 1.1f;
+// a split plan is taken only when it is predicted this much faster: on short
+// segments the model is optimistic (a chunk at base 1536 predicted 4 % faster
+// measured 18 % slower; at base 3584 predicted 7 %, measured 6 %)
+constexpr float PF_PLAN_MIN_GAIN = 0.90f;
+
+// Completion time of the segments when the hardware hands them, in launch
+// order, to `slots` cluster slots (each to the slot that frees first).
+float plan_makespan(const float* cost, int n, int slots) {
+  float fin[128] = {};
+  float makespan = 0.f;
+  for (int i = 0; i < n; ++i) {
+    int s = 0;
+    for (int k = 1; k < slots && k < 128; ++k)
+      if (fin[k] < fin[s]) s = k;
+    fin[s] += cost[i];
+    makespan = std::max(makespan, fin[s]);
+  }
+  return makespan;
+}
+}  // namespace
+
+size_t prefill_workspace_bytes() { return PF_QWS_BYTES + PF_PART_BYTES + PF_TICKET_BYTES; }
+
+std::atomic<int> g_prefill_split_mode{LISA_PREFILL_SPLIT_AUTO};
+
+// Splits the chunk's (query pair, head) units into the cluster segments of
+// the attention grid. A unit covers key tiles [0, n); split in two it becomes
+// [0, a) (launched with the whole units, heaviest first) and [a, n) (launched
+// after all of them), which fills the SMs a one-cluster-per-unit grid leaves
+// idle: 48 units on 74 cluster slots. The split point is one fraction of n
+// for all units, chosen by simulating the dispatch; a is at most the first
+// query row's position / 128, so every row sees a key in both ranges.
+void plan_segments(PrefillParams& p, int num_sms, int mode) {
+  const int n_qt = (p.rows + PF_BM - 1) / PF_BM;
+  const int n_pairs = (n_qt + 1) / 2;
+  const int slots = std::max(1, std::min(128, num_sms / 2));
+  int n_unit = 0, un[PF_MAX_UNITS], amax[PF_MAX_UNITS], uid[PF_MAX_UNITS];
+  for (int qp = n_pairs - 1; qp >= 0; --qp) {
+    const uint32_t pair_end = (uint32_t)std::min(qp * 2 * PF_BM + 2 * PF_BM, p.rows);
+    const uint32_t n = (p.base + pair_end + PF_BN - 1) / PF_BN;
+    for (int h = 0; h < QH; ++h) {
+      un[n_unit] = (int)n;
+      amax[n_unit] = (int)((p.base + (uint32_t)(qp * 2 * PF_BM)) / PF_BN);
+      uid[n_unit] = (qp << 8) | h;
+      ++n_unit;
+    }
+  }
+  // candidate split fractions in 1/20 steps; 0 = no split
+  int best_f = 0;
+  float best_t = 0.f, unsplit_t = 0.f;
+  for (int f = 0; f <= 17; ++f) {
+    if (f != 0 && f < 10) continue;
+    float cost[PF_MAX_SEGS], shorts[PF_MAX_UNITS];
+    int n = 0, n_short = 0;
+    for (int u = 0; u < n_unit; ++u) {
+      const int a = f ? std::min(amax[u], (un[u] * f + 10) / 20) : 0;
+      if (f && a >= 2 && un[u] - a >= 2) {
+        cost[n++] = a * PF_PLAN_BUSY + PF_PLAN_FIXED + PF_PLAN_SPLIT;
+        shorts[n_short++] = (un[u] - a) * PF_PLAN_BUSY + PF_PLAN_FIXED + PF_PLAN_SPLIT;
+      } else {
+        cost[n++] = un[u] + PF_PLAN_FIXED;
+      }
+    }
+    for (int i = 0; i < n_short; ++i) cost[n++] = shorts[i];
+    const float t = plan_makespan(cost, n, slots);
+    if (f == 0 || t < best_t) {
+      best_t = t;
+      best_f = f;
+    }
+    if (f == 0) unsplit_t = t;
+  }
+  if (best_t > PF_PLAN_MIN_GAIN * unsplit_t) best_f = 0;
+  if (mode == LISA_PREFILL_SPLIT_NEVER) best_f = 0;
+  if (mode == LISA_PREFILL_SPLIT_ALWAYS) best_f = 14;
+  int n = 0;
+  uint32_t s_lo[PF_MAX_UNITS], s_hi[PF_MAX_UNITS];
+  uint16_t s_unit[PF_MAX_UNITS];
+  int n_short = 0;
+  for (int u = 0; u < n_unit; ++u) {
+    const int a = best_f ? std::min(amax[u], (un[u] * best_f + 10) / 20) : 0;
+    if (best_f && a >= 2 && un[u] - a >= 2) {
+      p.seg_lo[n] = 0;
+      p.seg_hi[n] = (uint32_t)a;
+      p.seg_unit[n++] = (uint16_t)(uid[u] | 0x1000);
+      s_lo[n_short] = (uint32_t)a;
+      s_hi[n_short] = (uint32_t)un[u];
+      s_unit[n_short++] = (uint16_t)(uid[u] | 0x1000);
+    } else {
+      p.seg_lo[n] = 0;
+      p.seg_hi[n] = (uint32_t)un[u];
+      p.seg_unit[n++] = (uint16_t)uid[u];
+    }
+  }
+  for (int i = 0; i < n_short; ++i) {
+    p.seg_lo[n] = s_lo[i];
+    p.seg_hi[n] = s_hi[i];
+    p.seg_unit[n++] = s_unit[i];
+  }
+  p.n_seg = n;
+}
+
+#ifdef LISA_PREFILL_TRACE
+unsigned long long* g_prefill_trace = nullptr;  // debug builds: set by a trace harness
+#endif
 
 cudaError_t launch_prefill(const PrefillParams& p_in, int num_sms, cudaStream_t stream) {
-  (void)num_sms;
   PrefillParams p = p_in;
+#ifdef LISA_PREFILL_TRACE
+  p.trace = g_prefill_trace;
+#endif
   host_inv_freq(p.inv_freq);
+  p.part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(p.q_ws) + PF_QWS_BYTES);
+  p.tickets = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(p.q_ws) + PF_QWS_BYTES + PF_PART_BYTES);
+  plan_segments(p, num_sms, g_prefill_split_mode.load(std::memory_order_relaxed));
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -637,12 +859,18 @@ cudaError_t launch_prefill(const PrefillParams& p_in, int num_sms, cudaStream_t 
       lisa_encode_rows_map(&to, p.gated_out, (uint32_t)p.rows, OROW, 4, QH, HD, PF_BM) != 0 ||
       (p.in_bf16 && lisa_encode_rows_map(&tg, p.q_gate, (uint32_t)p.rows, QROW, 8, QH, 512, PF_BM) != 0))
     return cudaErrorInvalidValue;
-  const int n_qt = (p.rows + PF_BM - 1) / PF_BM;
-  const int n_pairs = (n_qt + 1) / 2;
-  cfg.gridDim = dim3(n_pairs * QH * 2);
+  cfg.gridDim = dim3(p.n_seg * 2);
   cfg.blockDim = dim3(PF_THREADS);
   cfg.dynamicSmemBytes = PF_SMEM_BYTES;
   return cudaLaunchKernelEx(&cfg, prefill_attn_kernel, tq, tk, tv, tg, to, p);
 }
 
 }  // namespace lisa
+
+#pragma GCC visibility push(default)
+extern "C" int lisa_attn_debug_prefill_split(int mode) {
+  if (mode != LISA_PREFILL_SPLIT_AUTO && mode != LISA_PREFILL_SPLIT_NEVER && mode != LISA_PREFILL_SPLIT_ALWAYS)
+    return LISA_EINVAL;
+  return lisa::g_prefill_split_mode.exchange(mode);
+}
+#pragma GCC visibility pop

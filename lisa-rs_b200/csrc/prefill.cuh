@@ -18,6 +18,10 @@ int lisa_encode_rows_map(CUtensorMap* map, const void* base, uint32_t rows, uint
 namespace lisa {
 
 constexpr int PF_MAX_ROWS = 512;
+// (query row pair, head) units of a chunk: at most 2 pairs x 24 heads; each is
+// one cluster, or two clusters over consecutive key ranges (split units).
+constexpr int PF_MAX_UNITS = 48;
+constexpr int PF_MAX_SEGS = 2 * PF_MAX_UNITS;
 
 struct PrefillParams {
   const void* q_gate;  // [rows][24][512]
@@ -35,6 +39,15 @@ struct PrefillParams {
   uint16_t* q_ws;     // workspace: normalised query, bf16 [24 heads][512 rows][256]
   uint16_t* gated_out;  // [rows][6144]
   int* err;
+  // Key-range segments, one per cluster in launch order (filled by
+  // launch_prefill): key tiles [seg_lo, seg_hi) of unit seg_unit (bits 0-7
+  // head, 8-11 query pair, bit 12 set when the unit is split in two).
+  int n_seg;
+  uint32_t seg_lo[PF_MAX_SEGS];
+  uint32_t seg_hi[PF_MAX_SEGS];
+  uint16_t seg_unit[PF_MAX_SEGS];
+  float* part;          // split partials, per (unit, CTA rank): O [64][128 rows][4] f32, then max / sum per row
+  uint32_t* tickets;    // per (unit, CTA rank): arrival count, then the partial-ready flag
   float inv_freq[32];  // filled by launch_prefill
 #if defined(LISA_PREFILL_TRACE) || defined(LISA_PREFILL_OBSERVE)
   unsigned long long* trace;  // debug builds only
