@@ -13,11 +13,13 @@
 // B200 layout. The kernel is bound by streaming the packed weights from HBM
 // (K/2 + K/16 bytes per row). One launch covers up to four projections of the
 // same x (q, k, v fused). One persistent CTA per SM: a producer warp moves
-// blocks of 16 consecutive rows (packed words, scales, biases: three bulk
-// copies) through a ring of shared-memory stages, and 16 consumer warps take
-// one row each: lane l dequantises the 32-element chunks l, l + 32, ... (a
+// blocks of 32 (or 16) consecutive rows (packed words, scales, biases: three
+// bulk copies) through a ring of shared-memory stages, and one consumer warp
+// per two rows of a block: lane l dequantises the 32-element chunks l, l + 32, ... (a
 // nibble dropped into the mantissa of 2^23, minus 2^23: no int -> float
-// conversion) and dots them with x in packed f32x2 FMAs. x is staged in shared
+// conversion) and dots them with x in packed f32x2 FMAs, each x chunk read
+// from shared memory once for both rows (x, not the weights, is most of the
+// shared-memory traffic: 32 f32 per 16 bytes of packed weights). x is staged in shared
 // memory as f32, one 32-element chunk per 36-float slot, so a quarter warp's
 // 16-byte reads of 8 consecutive chunks hit 8 disjoint bank quads; the
 // per-chunk sums of x (for the bias term) sit after it.
@@ -34,7 +36,14 @@ namespace lisa {
 
 namespace {
 
-constexpr int QMV_BR = 16;     // rows per stage = consumer warps
+// Rows per stage (BR): 32 for M <= 2 when x and two such stages fit in shared
+// memory (K <= 6144 at M = 1), else 16; the verify shapes always take 16, as
+// their larger accumulators would spill with 16 consumer warps. Measured at
+// M = 1, K = 5120 (q/k/v fused): 14.7 us with 32 rows and 2 rows per warp,
+// 16.0 with 16 and 2, 15.3 with 32 and 4, 16.6 with 16 and 4, 17.5 with one
+// row per warp.
+constexpr int QMV_RPW = 2;  // rows per consumer warp: each x chunk read from shared memory serves both
+__host__ __device__ constexpr int qmv_cw(int br) { return br / QMV_RPW; }  // consumer warps
 constexpr int QMV_STAGES = 4;  // weight blocks in flight per SM (fewer when x is large)
 constexpr int QMV_MAX_M = LISA_ATTN_QMV_MAX_ROWS;
 constexpr int QMV_MAX_PROJ = LISA_ATTN_QMV_MAX_PROJ;
@@ -50,7 +59,7 @@ struct QmvProj {
 };
 
 struct QmvParams {
-  int m, k, n_proj, groups;  // groups: blocks of QMV_BR rows over all projections
+  int m, k, n_proj, groups;  // groups: blocks of rows (one stage each) over all projections
   int stages;                // ring depth (2..QMV_STAGES, as shared memory allows)
   const uint16_t* x;         // [M][K] bf16
   QmvProj proj[QMV_MAX_PROJ];
@@ -61,11 +70,12 @@ struct QmvParams {
 // Persistent, one CTA per SM: a producer warp streams blocks of QMV_BR
 // consecutive weight rows of the projections (packed words, scales and biases
 // by bulk copies) through a ring of up to QMV_STAGES shared-memory stages
-// (mbarrier full / empty), and QMV_BR consumer warps dequantise and dot them
+// (mbarrier full / empty), and QMV_BR / 2 consumer warps dequantise and dot them
 // against x (staged once per CTA as f32). The ring keeps the stages' weights
 // in flight per SM whatever the registers.
-template <int M>
-__global__ void __launch_bounds__(32 * (QMV_BR + 1), 1) qmv_u4_kernel(const __grid_constant__ QmvParams p) {
+template <int M, int QMV_BR>
+__global__ void __launch_bounds__(32 * (qmv_cw(QMV_BR) + 1), 1) qmv_u4_kernel(const __grid_constant__ QmvParams p) {
+  constexpr int QMV_CW = qmv_cw(QMV_BR);
   extern __shared__ __align__(16) uint8_t qmv_smem_raw[];
   const int K = p.k;
   const int chunks = K / 32, groups_k = K / 64;
@@ -86,13 +96,13 @@ __global__ void __launch_bounds__(32 * (QMV_BR + 1), 1) qmv_u4_kernel(const __gr
   if (threadIdx.x == 0) {
     for (int s = 0; s < n_st; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], QMV_BR);
+      mbar_init(&empty[s], QMV_CW);
     }
     fence_mbar_init();
   }
   __syncthreads();
 
-  if (warp == QMV_BR) {
+  if (warp == QMV_CW) {
     // ---------------- producer ----------------
     // The weights are never written by a kernel: streaming starts before the
     // wait on the previous kernel (which may produce x).
@@ -136,7 +146,7 @@ __global__ void __launch_bounds__(32 * (QMV_BR + 1), 1) qmv_u4_kernel(const __gr
   pdl_wait_primary();
   pdl_launch_dependents();
   // x arrives as 16-byte vectors of 8 bf16 (a run of 8 never crosses a row)
-  for (int e8 = threadIdx.x; e8 < M * K / 8; e8 += 32 * QMV_BR) {
+  for (int e8 = threadIdx.x; e8 < M * K / 8; e8 += 32 * QMV_CW) {
     const uint4 v = __ldg(reinterpret_cast<const uint4*>(p.x) + e8);
     const int m = (8 * e8) / K, k = 8 * e8 - m * K;
     float4* dst = reinterpret_cast<float4*>(xs + ((size_t)m * chunks + (k >> 5)) * QMV_SLOT + (k & 31));
@@ -144,18 +154,19 @@ __global__ void __launch_bounds__(32 * (QMV_BR + 1), 1) qmv_u4_kernel(const __gr
     dst[0] = make_float4(a.x, a.y, b.x, b.y);
     dst[1] = make_float4(c2.x, c2.y, d.x, d.y);
   }
-  named_bar_sync(1, 32 * QMV_BR);
-  for (int e = threadIdx.x; e < M * chunks; e += 32 * QMV_BR) {
+  named_bar_sync(1, 32 * QMV_CW);
+  for (int e = threadIdx.x; e < M * chunks; e += 32 * QMV_CW) {
     const float* sl = xs + (size_t)e * QMV_SLOT;
     float sum = 0.f;
 #pragma unroll 8
     for (int i = 0; i < 32; ++i) sum += sl[i];
     xsum[e] = sum;
   }
-  named_bar_sync(1, 32 * QMV_BR);
+  named_bar_sync(1, 32 * QMV_CW);
 
-  // Consumer warp w takes row w of each stage; lane l the 32-element chunks
-  // l, l + 32, ... of K.
+  // Consumer warp w takes rows QMV_RPW * w .. of each stage; lane l the
+  // 32-element chunks l, l + 32, ... of K, each x chunk read once for all of
+  // the warp's rows.
   int it = 0;
   for (int blk = blockIdx.x; blk < n_blocks; blk += gridDim.x, ++it) {
     const int s = it % n_st;
@@ -163,56 +174,74 @@ __global__ void __launch_bounds__(32 * (QMV_BR + 1), 1) qmv_u4_kernel(const __gr
     int pi = 0;
     while (pi + 1 < p.n_proj && blk >= p.proj[pi + 1].grp0) ++pi;
     const QmvProj& pr = p.proj[pi];
-    const int row = (blk - pr.grp0) * QMV_BR + warp;
+    const int lr0 = warp * QMV_RPW;  // first local row of this warp
+    const int row0 = (blk - pr.grp0) * QMV_BR + lr0;
     const uint8_t* st = stages + (size_t)s * stage_bytes;
-    if (row < pr.n) {
-      const uint4* wrow = reinterpret_cast<const uint4*>(st + (size_t)warp * row_bytes);
-      const uint16_t* scr = reinterpret_cast<const uint16_t*>(st + QMV_BR * row_bytes) + (size_t)warp * groups_k;
+    if (row0 < pr.n) {
+      const uint16_t* scr = reinterpret_cast<const uint16_t*>(st + QMV_BR * row_bytes) + (size_t)lr0 * groups_k;
       const uint16_t* bir =
-          reinterpret_cast<const uint16_t*>(st + QMV_BR * row_bytes + sg_bytes) + (size_t)warp * groups_k;
-      float acc[M];
+          reinterpret_cast<const uint16_t*>(st + QMV_BR * row_bytes + sg_bytes) + (size_t)lr0 * groups_k;
+      float acc[QMV_RPW][M];
 #pragma unroll
-      for (int m = 0; m < M; ++m) acc[m] = 0.f;
+      for (int j = 0; j < QMV_RPW; ++j)
+#pragma unroll
+        for (int m = 0; m < M; ++m) acc[j][m] = 0.f;
       for (int c = lane; c < chunks; c += 32) {
-        const uint4 w4 = wrow[c];
         // nibble 2i is the low half of byte i, nibble 2i+1 the high half; a
         // nibble placed in the low mantissa bits of 2^23 is 2^23 + q, and
         // 2^23 + q - 2^23 = q exactly (no int -> float conversion)
-        float2 qv[16];
+        float2 qv[QMV_RPW][16];
 #pragma unroll
-        for (int wq = 0; wq < 4; ++wq) {
-          const uint32_t word = (&w4.x)[wq];
-          const uint32_t lo = word & 0x0F0F0F0Fu, hi = (word >> 4) & 0x0F0F0F0Fu;
+        for (int j = 0; j < QMV_RPW; ++j) {
+          const uint4 w4 = reinterpret_cast<const uint4*>(st + (size_t)(lr0 + j) * row_bytes)[c];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const uint32_t sel = (uint32_t)i | 0x7540u;  // byte i of the nibbles, then 00 00 4B
-            qv[4 * wq + i] = fadd2(make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, sel)),
-                                               __uint_as_float(__byte_perm(hi, 0x4B000000u, sel))),
-                                   make_float2(-8388608.0f, -8388608.0f));
+          for (int wq = 0; wq < 4; ++wq) {
+            const uint32_t word = (&w4.x)[wq];
+            const uint32_t lo = word & 0x0F0F0F0Fu, hi = (word >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint32_t sel = (uint32_t)i | 0x7540u;  // byte i of the nibbles, then 00 00 4B
+              qv[j][4 * wq + i] = fadd2(make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, sel)),
+                                                    __uint_as_float(__byte_perm(hi, 0x4B000000u, sel))),
+                                        make_float2(-8388608.0f, -8388608.0f));
+            }
           }
         }
-        const float scale = bf16_bits_to_f32(scr[c >> 1]), bias = bf16_bits_to_f32(bir[c >> 1]);
 #pragma unroll
         for (int m = 0; m < M; ++m) {
           const float4* xm = reinterpret_cast<const float4*>(xs + ((size_t)m * chunks + c) * QMV_SLOT);
-          float2 dot = make_float2(0.f, 0.f);
+          float2 dot[QMV_RPW];
+#pragma unroll
+          for (int j = 0; j < QMV_RPW; ++j) dot[j] = make_float2(0.f, 0.f);
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
             const float4 x4 = xm[q];
-            dot = ffma2(make_float2(x4.x, x4.y), qv[2 * q], dot);
-            dot = ffma2(make_float2(x4.z, x4.w), qv[2 * q + 1], dot);
+#pragma unroll
+            for (int j = 0; j < QMV_RPW; ++j) {
+              dot[j] = ffma2(make_float2(x4.x, x4.y), qv[j][2 * q], dot[j]);
+              dot[j] = ffma2(make_float2(x4.z, x4.w), qv[j][2 * q + 1], dot[j]);
+            }
           }
-          acc[m] += fmaf(scale, dot.x + dot.y, bias * xsum[m * chunks + c]);
+          const float xsc = xsum[m * chunks + c];
+#pragma unroll
+          for (int j = 0; j < QMV_RPW; ++j) {
+            const float scale = bf16_bits_to_f32(scr[j * groups_k + (c >> 1)]);
+            const float bias = bf16_bits_to_f32(bir[j * groups_k + (c >> 1)]);
+            acc[j][m] += fmaf(scale, dot[j].x + dot[j].y, bias * xsc);
+          }
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
 #pragma unroll
-      for (int m = 0; m < M; ++m) {
-        float v = acc[m];
+      for (int j = 0; j < QMV_RPW; ++j) {
 #pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-        if (lane == 0) pr.out[(size_t)m * pr.n + row] = v;
+        for (int m = 0; m < M; ++m) {
+          float v = acc[j][m];
+#pragma unroll
+          for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+          if (lane == 0 && row0 + j < pr.n) pr.out[(size_t)m * pr.n + row0 + j] = v;
+        }
       }
     } else {
       __syncwarp();
@@ -230,24 +259,25 @@ namespace {
 constexpr size_t kSmemMax = 227 * 1024;
 
 size_t qmv_x_bytes(int m, int k) { return ((size_t)m * (k / 32) * (QMV_SLOT + 1) * sizeof(float) + 127) & ~size_t(127); }
-size_t qmv_stage_bytes(int k) {
-  const size_t sg = ((size_t)QMV_BR * (k / 64) * 2 + 15) & ~size_t(15);
-  return ((size_t)QMV_BR * k / 2 + 2 * sg + 127) & ~size_t(127);
+size_t qmv_stage_bytes(int br, int k) {
+  const size_t sg = ((size_t)br * (k / 64) * 2 + 15) & ~size_t(15);
+  return ((size_t)br * k / 2 + 2 * sg + 127) & ~size_t(127);
 }
-int qmv_stages(int m, int k) {
+int qmv_stages(int br, int m, int k) {
   const size_t room = kSmemMax - qmv_x_bytes(m, k) - 2 * QMV_STAGES * sizeof(uint64_t);
-  return (int)std::max<size_t>(2, std::min<size_t>(QMV_STAGES, room / qmv_stage_bytes(k)));
+  return (int)std::max<size_t>(2, std::min<size_t>(QMV_STAGES, room / qmv_stage_bytes(br, k)));
 }
-size_t qmv_smem_bytes(int m, int k) {
-  const int st = qmv_stages(m, k);
-  return qmv_x_bytes(m, k) + st * qmv_stage_bytes(k) + 2 * st * sizeof(uint64_t);
+size_t qmv_smem_bytes(int br, int m, int k) {
+  const int st = qmv_stages(br, m, k);
+  return qmv_x_bytes(m, k) + st * qmv_stage_bytes(br, k) + 2 * st * sizeof(uint64_t);
 }
+int qmv_rows_per_stage(int m, int k) { return m <= 2 && qmv_smem_bytes(32, m, k) <= kSmemMax ? 32 : 16; }
 
-template <int M>
+template <int M, int BR>
 cudaError_t launch_m(cudaLaunchConfig_t& cfg, const QmvParams& p) {
   static SmemAttr attr_once;  // per kernel and device, for the largest request
-  const cudaError_t e = attr_once.ensure(qmv_u4_kernel<M>, (int)kSmemMax);
-  return e == cudaSuccess ? cudaLaunchKernelEx(&cfg, qmv_u4_kernel<M>, p) : e;
+  const cudaError_t e = attr_once.ensure(qmv_u4_kernel<M, BR>, (int)kSmemMax);
+  return e == cudaSuccess ? cudaLaunchKernelEx(&cfg, qmv_u4_kernel<M, BR>, p) : e;
 }
 
 }  // namespace
@@ -262,21 +292,22 @@ extern "C" int lisa_attn_qmv_u4(int n_proj, const lisa_attn_q4_proj* projs, int 
   p.k = k;
   p.n_proj = n_proj;
   p.x = x;
-  int blocks = 0;  // blocks of QMV_BR rows over all projections
+  const int br = qmv_rows_per_stage(rows, k);
+  int blocks = 0;  // blocks of br rows over all projections
   for (int i = 0; i < n_proj; ++i) {
     const lisa_attn_q4_proj& q = projs[i];
     if (!q.packed || !q.scales || !q.biases || !q.out || q.n < 1) return LISA_EINVAL;
     if ((uintptr_t)q.packed & 15) return LISA_EINVAL;  // bulk copies of packed rows
     p.proj[i] = QmvProj{static_cast<const uint32_t*>(q.packed), q.scales, q.biases, q.out, q.n, blocks};
-    blocks += (q.n + QMV_BR - 1) / QMV_BR;
+    blocks += (q.n + br - 1) / br;
   }
   p.groups = blocks;
-  p.stages = qmv_stages(rows, k);
-  if (qmv_smem_bytes(rows, k) > kSmemMax) return LISA_EINVAL;  // x and two weight stages must fit
+  p.stages = qmv_stages(br, rows, k);
+  if (qmv_smem_bytes(br, rows, k) > kSmemMax) return LISA_EINVAL;  // x and two weight stages must fit
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(std::min(current_device_sms(), blocks));
-  cfg.blockDim = dim3(32 * (QMV_BR + 1));
-  cfg.dynamicSmemBytes = qmv_smem_bytes(rows, k);
+  cfg.blockDim = dim3(32 * (qmv_cw(br) + 1));
+  cfg.dynamicSmemBytes = qmv_smem_bytes(br, rows, k);
   cfg.stream = static_cast<cudaStream_t>(stream);
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -285,10 +316,10 @@ extern "C" int lisa_attn_qmv_u4(int n_proj, const lisa_attn_q4_proj* projs, int 
   cfg.numAttrs = 1;
   cudaError_t e;
   switch (rows) {
-    case 1: e = launch_m<1>(cfg, p); break;
-    case 2: e = launch_m<2>(cfg, p); break;
-    case 3: e = launch_m<3>(cfg, p); break;
-    default: e = launch_m<4>(cfg, p); break;
+    case 1: e = br == 32 ? launch_m<1, 32>(cfg, p) : launch_m<1, 16>(cfg, p); break;
+    case 2: e = br == 32 ? launch_m<2, 32>(cfg, p) : launch_m<2, 16>(cfg, p); break;
+    case 3: e = launch_m<3, 16>(cfg, p); break;
+    default: e = launch_m<4, 16>(cfg, p); break;
   }
   return e == cudaSuccess ? LISA_OK : LISA_ECUDA;
 }
