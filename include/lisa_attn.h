@@ -155,7 +155,8 @@ int lisa_attn_kv_restore(lisa_attn_ctx* ctx, const void* src, size_t src_bytes, 
 
 /* Device-side error flag of the context (bounded waits that gave up).
  * Synchronises the context's device; returns LISA_OK, LISA_ETIMEOUT or
- * LISA_ECUDA, and clears the flag. */
+ * LISA_ECUDA, and clears the flag (and, after an error, the prefill's
+ * split-merge tickets, so that later prefill calls start clean). */
 int lisa_attn_check_device_error(lisa_attn_ctx* ctx);
 
 /* ---- split-KV window entry points (multi-GPU) ------------------------------

@@ -745,6 +745,8 @@ float plan_makespan(const float* cost, int n, int slots) {
 }  // namespace
 
 size_t prefill_workspace_bytes() { return PF_QWS_BYTES + PF_PART_BYTES + PF_TICKET_BYTES; }
+size_t prefill_ticket_offset() { return PF_QWS_BYTES + PF_PART_BYTES; }
+size_t prefill_ticket_bytes() { return PF_TICKET_BYTES; }
 
 std::atomic<int> g_prefill_split_mode{LISA_PREFILL_SPLIT_AUTO};
 

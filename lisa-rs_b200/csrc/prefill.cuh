@@ -56,6 +56,11 @@ struct PrefillParams {
 
 // Bytes of device workspace launch_prefill needs.
 size_t prefill_workspace_bytes();
+// Byte offset and size of the split-merge tickets inside that workspace; a
+// launch that gave up (device error) may leave them non-zero, and the
+// context's error check clears them.
+size_t prefill_ticket_offset();
+size_t prefill_ticket_bytes();
 
 // Prologue (q norm/RoPE into q_ws, K/V append) then the tcgen05 attention.
 cudaError_t launch_prefill(const PrefillParams& p, int num_sms, cudaStream_t stream);

@@ -396,7 +396,12 @@ int lisa_attn_check_device_error(lisa_attn_ctx* c) {
   if (cudaDeviceSynchronize() != cudaSuccess) return LISA_ECUDA;
   int h = 0;
   if (cudaMemcpy(&h, c->err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return LISA_ECUDA;
-  if (h) cudaMemset(c->err, 0, sizeof(int));
+  if (h) {
+    cudaMemset(c->err, 0, sizeof(int));
+    // a prefill launch that gave up may have left a split-merge ticket taken
+    cudaMemset(static_cast<uint8_t*>(c->prefill_ws) + prefill_ticket_offset(), 0, prefill_ticket_bytes());
+    cudaDeviceSynchronize();
+  }
   return h ? LISA_ETIMEOUT : LISA_OK;
 }
 
