@@ -310,6 +310,14 @@ int lisa_attn_debug_wait_fault(uint32_t wait_limit_us, int withhold_loads);
 #define LISA_PREFILL_SPLIT_ALWAYS 2
 int lisa_attn_debug_prefill_split(int mode);
 
+/* Host only, no device work: the cluster segments the prefill planner gives a
+ * chunk of `rows` rows at `base` on a device with num_sms SMs under `mode`, in
+ * launch order: key tiles [seg_lo, seg_hi) of unit seg_unit (bits 0-7 head,
+ * 8-11 query row pair, bit 12 set for a split unit). cap >= 96. Returns the
+ * segment count, or LISA_EINVAL. */
+int lisa_attn_debug_prefill_plan(uint32_t base, int rows, int num_sms, int mode, uint32_t* seg_lo,
+                                 uint32_t* seg_hi, uint16_t* seg_unit, int cap);
+
 /* ---- affine-u4 projections (QMV) --------------------------------------------
  * The quantised matrix-vector products around the attention layer for the
  * decode (rows = 1) and verify (rows = 3) shapes: q4_qmv_fast / fused2/3/4

@@ -870,6 +870,24 @@ cudaError_t launch_prefill(const PrefillParams& p_in, int num_sms, cudaStream_t 
 }  // namespace lisa
 
 #pragma GCC visibility push(default)
+extern "C" int lisa_attn_debug_prefill_plan(uint32_t base, int rows, int num_sms, int mode, uint32_t* seg_lo,
+                                            uint32_t* seg_hi, uint16_t* seg_unit, int cap) {
+  if (rows < 1 || rows > lisa::PF_MAX_ROWS || num_sms < 2 || !seg_lo || !seg_hi || !seg_unit ||
+      cap < lisa::PF_MAX_SEGS || base > (1u << 30) ||
+      (mode != LISA_PREFILL_SPLIT_AUTO && mode != LISA_PREFILL_SPLIT_NEVER && mode != LISA_PREFILL_SPLIT_ALWAYS))
+    return LISA_EINVAL;
+  lisa::PrefillParams p = {};
+  p.base = base;
+  p.rows = rows;
+  lisa::plan_segments(p, num_sms, mode);
+  for (int i = 0; i < p.n_seg; ++i) {
+    seg_lo[i] = p.seg_lo[i];
+    seg_hi[i] = p.seg_hi[i];
+    seg_unit[i] = p.seg_unit[i];
+  }
+  return p.n_seg;
+}
+
 extern "C" int lisa_attn_debug_prefill_split(int mode) {
   if (mode != LISA_PREFILL_SPLIT_AUTO && mode != LISA_PREFILL_SPLIT_NEVER && mode != LISA_PREFILL_SPLIT_ALWAYS)
     return LISA_EINVAL;

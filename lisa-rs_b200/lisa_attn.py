@@ -72,6 +72,7 @@ SIGNATURES = {
     "lisa_attn_noalloc_check_device_error": (_i32, []),
     "lisa_attn_debug_wait_fault": (_i32, [_u32, _i32]),
     "lisa_attn_debug_prefill_split": (_i32, [_i32]),
+    "lisa_attn_debug_prefill_plan": (_i32, [_u32, _i32, _i32, _i32, _P, _P, _P, _i32]),
     "lisa_attn_qmv_u4": (_i32, [_i32, _P, _i32, _i32, _P, _P]),
     "lisa_attn_gdn_recurrence": (_i32, [_i32, _i32, _i32, _P, _P, _P, _P, _P, _P, _P, _P, _sz, _P]),
     "lisa_attn_st_open": (_i32, [ctypes.c_char_p, ctypes.POINTER(_P)]),
